@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Headline benchmark: lowbit's W4A16 decode GEMM (M=1, N=11008, K=4096, int4 g128 asym)
+on B200, reported as weight GB/s (BASELINE.json metric and configs[0]).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Our arm ("ours"):
+  * a step = one fused dequant+GEMM of the step's weight matrix (11008x4096
+    int4) against X [1, 4096] fp32; with N>1 ranks each rank owns N/P weight
+    rows and the step ends with an NCCL all-gather of Y (column parallelism);
+  * inputs resident in HBM; consecutive steps read different copies of the
+    weights from a rotating pool larger than 2x L2 (every step streams its
+    weights from HBM, like successive layers in decode);
+  * the K timed steps are captured in one CUDA graph and replayed, bracketed
+    by barrier + synchronize, timed with CUDA events, max over ranks;
+  * `e2e`: the same step through the public API (lowbit_b200.gemm_w4a16) with
+    X copied from pinned host memory and Y read back to pinned host memory
+    every step, synchronised per step.
+Reference arm: lowbit's own CPU kernels (compiled from the reference's sources
+into oracle/_ref) on all host cores, same config, same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M, N, K = 1, 11008, 4096
+L2_BYTES = 126 * 2**20
+METRIC = "M=1 decode weight GB/s (W4A16 int4-g128 asym, N=11008, K=4096)"
+WORKLOAD = "W4A16 decode GEMM M=1 N=11008 K=4096, int4 g128 asym (BASELINE configs[0])"
+PUBLISHED_GBPS = 22.4  # reference README: W4A16 M=1 N=11008 K=4096 cold, AVX-512, 4 threads
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks() -> tuple[float, float, float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 0)),
+                "measured (MEASURED_PEAKS.json)")
+    return FALLBACK_HBM_GBS, 1590.0, 1400.0, "fallback (profiling recipe)"
+
+
+def inputs(m=M, n=N, k=K):
+    w = np.random.default_rng(0).standard_normal((n, k)).astype(np.float32)
+    x = np.random.default_rng(1).standard_normal((m, k)).astype(np.float32)
+    return x, w
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU is busy."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, pw, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [s.strip() for s in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                pw.append(float(f[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args) -> dict:
+    from lowbit_b200 import quantize_int4
+    from oracle import ref_lib
+    if not ref_lib.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/liblowbit_ref.so not built "
+                "(make -C oracle ref needs the reference sources)"}
+    x, w = inputs()
+    W = quantize_int4(w, asym=True)
+    threads = os.cpu_count() or 1
+    g = ref_lib.RefGemm("w4a16", x, W, threads)
+    info = g.info()
+    g.tune(budget_s=3.0)
+    pool = _host_pool(W)
+    for i in range(args.warmup):
+        g.w = pool[i % len(pool)]
+        g()
+    ts = []
+    for i in range(args.steps):
+        g.w = pool[i % len(pool)]
+        t0 = time.perf_counter()
+        g()
+        ts.append(time.perf_counter() - t0)
+    total = sum(ts)
+    gbps = W.nbytes / (total / args.steps) / 1e9
+    sample = (f"lowbit lb_gemm_w4a16 ({info['isa']}, openmp={info['openmp']}) M=1 N=11008 K=4096, "
+              f"{args.steps} calls, cold: {len(pool)} weight copies rotated, tuned params "
+              f"mr={g.params.mr} nr={g.params.nr} nb={g.params.nb} kb={g.params.kb}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbps, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": round(gbps / PUBLISHED_GBPS, 3), "dtype": "f32",
+        "data": "synthetic: W~N(0,1) seed 0, X~N(0,1) seed 1 (BASELINE configs[0])",
+        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "format": "w4a16",
+                   "parallelism": f"OpenMP {threads} threads on the host", "l2": "cold (rotating copies)"},
+        "cpu_baseline": {"value": round(gbps, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(gbps, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return line
+
+
+def _host_pool(W):
+    """Host weight copies exceeding 2x a generous LLC (the reference's cold mode, lb/bench.py:169-178)."""
+    from dataclasses import replace
+    copies = int(max(2, min(24, np.ceil((512 << 20) / W.nbytes))))
+    return [W] + [replace(W, qw=W.qw.copy(), scales=W.scales.copy(),
+                          zeros=None if W.zeros is None else W.zeros.copy()) for _ in range(copies - 1)]
+
+
+def cpu_baseline(budget_s: float = 10.0) -> dict:
+    """The reference's CPU kernel on the host cores, bounded sample (rank 0, N=1)."""
+    from lowbit_b200 import quantize_int4
+    from oracle import ref_lib
+    if not ref_lib.available():
+        return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref/liblowbit_ref.so not built"}
+    x, w = inputs()
+    W = quantize_int4(w, asym=True)
+    threads = os.cpu_count() or 1
+    g = ref_lib.RefGemm("w4a16", x, W, threads)
+    info = g.info()
+    g.tune(budget_s=3.0)
+    pool = _host_pool(W)
+    ts = []
+    t_end = time.perf_counter() + budget_s
+    i = 0
+    while time.perf_counter() < t_end or len(ts) < 5:
+        g.w = pool[i % len(pool)]
+        t0 = time.perf_counter()
+        g()
+        ts.append(time.perf_counter() - t0)
+        i += 1
+    med = statistics.median(ts)
+    return {"value": round(W.nbytes / med / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": f"lowbit lb_gemm_w4a16 ({info['isa']}, openmp={info['openmp']}) M=1 N=11008 K=4096, "
+                      f"median of {len(ts)} cold calls over {budget_s:.0f} s, tuned mr={g.params.mr} "
+                      f"nr={g.params.nr} nb={g.params.nb} kb={g.params.kb}"}
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    import lowbit_b200 as lb
+    from lowbit_b200 import kernels as Kn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    x, w = inputs()
+    W = lb.quantize_int4(w, asym=True)
+    Wl = W.shard(rank, world)
+    n_loc = Wl.n
+    wbytes_total = W.nbytes
+    wbytes_local = Wl.nbytes
+    copies = int(max(2, min(64, np.ceil(2 * L2_BYTES / wbytes_local) + 1)))
+    base = Wl.cuda(dev)
+    pool = [base] + [lb.Int4Weights(base.qw.clone(), base.scales.clone(), base.zeros.clone(), base.k)
+                     for _ in range(copies - 1)]
+    pool_mb = copies * wbytes_local / 2**20
+    xd = torch.from_numpy(x).to(dev)
+    prep = Kn._Prepared(xd, W.kp, n_loc)
+    yfull = torch.empty((world, M, n_loc), dtype=torch.float32, device=dev)
+
+    def gemv(i):
+        Kn.gemm_w4a16(prep.x, pool[i % copies], _prep=prep)
+
+    def step(i):
+        gemv(i)
+        if world > 1:
+            dist.all_gather_into_tensor(yfull, prep.y)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # correctness of the configuration being timed (oracle check, outside the timing)
+    if rank == 0:
+        from oracle import lbref as R
+        gemv(0)
+        torch.cuda.synchronize()
+        ref = R.gemm_w4a16_ref(x, Wl.qw, Wl.scales, Wl.zeros)
+        R.assert_close(prep.y.cpu().numpy(), ref, R.abs_bound(x, R.dequant_int4(Wl.qw, Wl.scales, Wl.zeros)), 1e-5)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier()
+
+    def capture(fn, steps):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                for i in range(steps):
+                    fn(i)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        return g
+
+    g_step = capture(step, args.steps)
+    g_gemv = capture(gemv, args.steps) if world > 1 else g_step
+    g_step.replay()  # graph warm-up (not timed)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                          if "CUDA_VISIBLE_DEVICES" in os.environ else local)
+    clocks.start()
+    # keep the GPU busy ~1.5 s so the sampler sees the clocks under this load
+    t_soak = time.perf_counter() + 1.5
+    while time.perf_counter() < t_soak:
+        g_gemv.replay()
+        torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    ev0.record()
+    g_step.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_step_local = ev0.elapsed_time(ev1) / args.steps
+
+    # kernel-only duration (no collective) for the roofline
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev2.record()
+    g_gemv.replay()
+    ev3.record()
+    torch.cuda.synchronize()
+    ms_kernel_local = ev2.elapsed_time(ev3) / args.steps
+    clk = clocks.stop()
+
+    t = torch.tensor([ms_step_local, ms_kernel_local], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step, ms_kernel = float(t[0]), float(t[1])
+
+    # end to end through the public API, host buffers (pinned) in and out every step
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    xdev = torch.empty((M, K), dtype=torch.float32, device=dev)
+    e2e_steps = max(args.steps // 4, 20)
+
+    def e2e_step(i):
+        xdev.copy_(xh, non_blocking=True)
+        y = lb.gemm_w4a16(xdev, pool[i % copies])
+        if world > 1:
+            dist.all_gather_into_tensor(yfull, y)
+            yh.copy_(yfull.permute(1, 0, 2).reshape(M, N), non_blocking=True)
+        else:
+            yh.copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for i in range(5):
+        e2e_step(i)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e2e_local = (time.perf_counter() - t0) / e2e_steps
+    te = torch.tensor([e2e_local], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te[0])
+
+    del g_step, g_gemv
+    status = Kn.device_status(reset=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    hbm, _, _, peak_src = peaks()
+    alg_bytes = wbytes_local + Kn_x_bytes(W.kp) + M * n_loc * 4
+    achieved = alg_bytes / (ms_kernel * 1e-3) / 1e9
+    value = wbytes_total / (ms_step * 1e-3) / 1e9
+    traffic = _ncu_traffic("w4a16_decode") if world == 1 else None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 6),
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": round(value / PUBLISHED_GBPS, 2), "dtype": "f32",
+        "data": "synthetic: W~N(0,1) seed 0, X~N(0,1) seed 1, quantized by quantize_int4(asym=True)",
+        "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "format": "w4a16",
+                   "parallelism": f"N-shard x{world}" + (" + NCCL all-gather of Y" if world > 1 else ""),
+                   "l2": f"inputs larger than L2: {copies} rotating weight copies ({pool_mb:.0f} MB/rank)",
+                   "timing": "K steps in one CUDA graph replay, CUDA events, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": peak_src,
+                     "alg_bytes_per_launch": alg_bytes, "kernel_us": round(ms_kernel * 1e3, 3)},
+        "e2e": {"value": round(wbytes_total / e2e_s / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4,
+                "us_per_step": round(e2e_s * 1e6, 2)},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+    return line
+
+
+def Kn_x_bytes(kp: int) -> int:
+    return M * kp * 4
+
+
+def _ncu_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return
+        print(json.dumps(run_reference(args)), flush=True)
+        return
+    line = run_ours(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

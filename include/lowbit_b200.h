@@ -1,0 +1,142 @@
+/*
+ * lowbit_b200 — C ABI of the B200 (sm_100a) fused dequantize + GEMM kernels.
+ *
+ * Every GEMM computes  Y[M,N] = X[M,Kp] . W[N,Kp]^T  (nn.Linear convention,
+ * one weight row per output feature), exactly like lowbit's CPU library
+ * (src/lowbit/csrc/lowbit.h:1-20).  The packed weight layouts are the
+ * reference's, byte for byte, so weights quantized by lowbit are consumed
+ * unchanged:
+ *
+ *   int4, group 128 : row n holds Kp/2 bytes; group g = bytes [64g, 64g+64).
+ *                     Byte j of a group holds element 128g+j in its low nibble
+ *                     and element 128g+64+j in its high nibble.  Codes are
+ *                     unsigned 0..15; value = (q - z) * s with
+ *                     z = zeros[n,g] (8 when zeros == NULL), s = scales[n,g].
+ *   MXFP4, block 32 : block b = bytes [16b, 16b+16); byte j holds element
+ *                     32b+j (low nibble) and 32b+16+j (high nibble) as OCP
+ *                     E2M1 codes; value = e2m1(q) * 2^(e8m0[n,b] - 127),
+ *                     e8m0 == 255 decodes to NaN.
+ *
+ * Conventions shared by every entry point below:
+ *   - all data pointers are DEVICE pointers (cudaMalloc / torch CUDA memory)
+ *     on the current device; X is fp32 [M,Kp] zero-padded to Kp, Y is fp32
+ *     [M,N] and is OVERWRITTEN (the reference memsets Y then accumulates,
+ *     src/lowbit/csrc/dispatch.c:168);
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); calls are
+ *     stream-ordered and return before the GPU work finishes;
+ *   - return value >= 0 is the kernel path that ran (LBC_PATH_*); negative
+ *     values are the reference's error codes (src/lowbit/csrc/dispatch.c:
+ *     160,205-208,270-286) plus CUDA-specific ones.
+ */
+#ifndef LOWBIT_B200_H
+#define LOWBIT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LBC_GROUP 128  /* int4 group size (elements)   — lowbit.h:31 */
+#define LBC_MXBLOCK 32 /* MXFP4 block size (elements)  — lowbit.h:32 */
+
+/* kernel paths (returned by the GEMM entry points, requested via params.isa) */
+#define LBC_PATH_AUTO (-1)
+#define LBC_PATH_SIMT 0    /* CUDA-core fp32 FMA (int32 dp4a for W4A8) */
+#define LBC_PATH_TCGEN05 1 /* tcgen05 tensor-core prefill path */
+
+/* error codes: -1..-3 keep the reference's meaning */
+#define LBC_ERR_SHAPE (-1)  /* M,N,Kp <= 0, Kp % block, NULL pointer */
+#define LBC_ERR_PARAMS (-2) /* tile parameters not supported ("tile not compiled") */
+#define LBC_ERR_ALLOC (-3)  /* device scratch allocation failed */
+#define LBC_ERR_CUDA (-5)   /* a CUDA call or launch failed (see lbc_last_error) */
+#define LBC_ERR_DEVICE (-6) /* current device is not sm_100 */
+#define LBC_ERR_TIMEOUT (-7) /* a bounded device-side wait gave up */
+
+/*
+ * Tuning parameters.  Same memory layout as the reference's lb_params
+ * (src/lowbit/csrc/lowbit.h:37-45) so a caller's struct passes unchanged;
+ * the fields are reinterpreted for the GPU.  Zero or negative = default.
+ *   isa      : kernel path, LBC_PATH_* (-1 auto; reference ISA ids >= 2 = auto)
+ *   mr       : tokens per pass of the SIMT kernels (1,2,4,8)
+ *   nr       : weight rows per pipeline tile of the SIMT kernels (1..32)
+ *   nb       : resident CTAs per SM for the SIMT kernels
+ *   kb       : split-K length in elements (multiple of 128), 0 = whole K
+ *   order    : TMA pipeline stages
+ *   nthreads : ignored (CPU thread count; meaningless on the GPU)
+ */
+typedef struct {
+    int isa;
+    int mr;
+    int nr;
+    int nb;
+    int kb;
+    int order;
+    int nthreads;
+} lbc_params;
+
+/* ---- library / device queries (replace lb_version / lb_cpu_isa / ...,
+ *      src/lowbit/csrc/lowbit.h:95-102) ---- */
+int lbc_version(void);
+/* 1 if the current device is sm_100 and this build has kernels for it */
+int lbc_device_ok(void);
+/* number of SMs of the current device (0 on error) */
+int lbc_sm_count(void);
+/* last CUDA error text recorded by this library (thread-local, never NULL) */
+const char *lbc_last_error(void);
+/* device status word of the current device: 0, or LBC_ERR_TIMEOUT after a
+ * bounded device-side wait gave up; reset != 0 clears it. Synchronous. */
+int lbc_device_status(int reset);
+
+/* ---- GEMMs ---- */
+
+/* W4A16: replaces lb_gemm_w4a16 (src/lowbit/csrc/lowbit.h:104-106,
+ * src/lowbit/csrc/dispatch.c:210-218). zeros may be NULL (symmetric, z=8). */
+int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw,
+                   const float *scales, const uint8_t *zeros, int N, float *y,
+                   const lbc_params *p, void *stream);
+
+/* MXFP4: replaces lb_gemm_mxfp4 (src/lowbit/csrc/lowbit.h:107-108,
+ * src/lowbit/csrc/dispatch.c:220-229). Kp % 32 == 0. */
+int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw,
+                   const uint8_t *e8m0, int N, float *y, const lbc_params *p,
+                   void *stream);
+
+/* W4A8 with fp32 X: per-token int8 quantization runs inside the call, as in
+ * lb_gemm_w4a8 (src/lowbit/csrc/lowbit.h:109-112, dispatch.c:270-286).
+ * `workspace` is caller-owned device scratch of at least
+ * lbc_gemm_w4a8_workspace_size(M, Kp) bytes (256-byte aligned); when NULL the
+ * call allocates and frees it stream-ordered (cudaMallocAsync), which mirrors
+ * the reference's internal scratch allocation. */
+size_t lbc_gemm_w4a8_workspace_size(int M, int Kp);
+int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw,
+                  const float *scales, const uint8_t *zeros, int N, float *y,
+                  const lbc_params *p, void *workspace, void *stream);
+
+/* W4A8 on pre-quantized activations: replaces lb_gemm_w4a8_q
+ * (src/lowbit/csrc/lowbit.h:113-116, dispatch.c:259-268). */
+int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum,
+                    int M, int Kp, const uint8_t *qw, const float *scales,
+                    const uint8_t *zeros, int N, float *y, const lbc_params *p,
+                    void *stream);
+
+/* Per-token symmetric int8 quantization, bit-identical to lb_quant_act_int8
+ * (src/lowbit/csrc/lowbit.h:117-119, dispatch.c:231-257): sc = amax/127
+ * (1 when amax == 0), q = clamp(rne(x/sc), -127, 127), asum[m,g] = sum of
+ * the group's codes. Returns 0 or a negative error. */
+int lbc_quant_act_int8(const float *x, int M, int Kp, int8_t *xq, float *xs,
+                       int32_t *asum, void *stream);
+
+/* Exact int32 group accumulators out[m,n,g] = sum_{k in g} (q-z)*xq[m,k]
+ * (debug/test), replaces lb_w4a8_group_acc (src/lowbit/csrc/lowbit.h:
+ * 120-123, dispatch.c:288-305). `isa` is accepted and ignored. */
+int lbc_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, int Kp,
+                       const uint8_t *qw, const uint8_t *zeros, int N,
+                       int32_t *out, int isa, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOWBIT_B200_H */

@@ -1,0 +1,374 @@
+// extern "C" entry points of liblowbit_b200.so (declared in include/lowbit_b200.h)
+// and the launch planner that turns (format, M, N, Kp, params) into a kernel
+// configuration. The reference's equivalents are the public functions of
+// src/lowbit/csrc/dispatch.c:205-305 and its tiling driver run() (:148-203).
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "../../include/lowbit_b200.h"
+#include "gemv_dispatch.cuh"
+#include "kernels.h"
+
+namespace lbc {
+// device status word (see common.cuh); one per device, address passed to kernels
+__device__ int g_status = 0;
+}
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail_cuda(const char *what, cudaError_t e) {
+  snprintf(g_err, sizeof g_err, "%s: %s", what, cudaGetErrorString(e));
+  return LBC_ERR_CUDA;
+}
+
+int fail(int code, const char *msg) {
+  snprintf(g_err, sizeof g_err, "%s", msg);
+  return code;
+}
+
+struct DevInfo {
+  int ok = 0, sms = 0, smem_optin = 0, smem_sm = 0;
+  int *status = nullptr;
+};
+
+DevInfo dev_info() {
+  static DevInfo cache[64];
+  static bool init[64] = {false};
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return DevInfo{};
+  if (!init[d]) {
+    DevInfo di;
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, d);
+    cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, d);
+    cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d);
+    cudaDeviceGetAttribute(&di.smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, d);
+    di.ok = (major == 10 && minor == 0);
+    if (di.ok && cudaGetSymbolAddress(reinterpret_cast<void **>(&di.status), lbc::g_status) != cudaSuccess) {
+      cudaGetLastError();
+      di.status = nullptr;
+    }
+    cache[d] = di;
+    init[d] = true;
+  }
+  return cache[d];
+}
+
+inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline int round_up(int a, int b) { return ceil_div(a, b) * b; }
+
+int check_shape(int M, int Kp, int N, int block) {
+  if (M <= 0 || N <= 0 || Kp <= 0 || Kp % block) return fail(LBC_ERR_SHAPE, "bad shape");
+  return 0;
+}
+
+// ------------------------------------------------------------------ planner
+struct GemvPlan {
+  int mt = 1, ch = 1, rt = 4, tpr = 32, nt = 256, tile_rows = 4, stages = 4;
+  int nsplit = 1, seg = 0, ctas_per_split = 1, ntiles = 1, passes = 1;
+  int threads = 288, smem = 0;
+};
+
+bool combo_ok(int fmt, int mt, int ch, int rt) {
+  if (rt != 1 && rt != 4) return false;
+  if (fmt == lbc::FMT_W4A8) {
+    if (ch == 1) return mt == 1 || mt == 2 || mt == 4 || mt == 8;
+    if (ch == 2) return mt == 1 || mt == 2 || mt == 4;
+    if (ch == 4) return mt == 1 || mt == 2;
+    return false;
+  }
+  if (ch == 1) return mt == 1 || mt == 2 || mt == 4;
+  if (ch == 2) return mt == 1 || mt == 2;
+  if (ch == 4) return mt == 1;
+  return false;
+}
+
+int occupancy(int fmt, int mt, int ch, int rt, int threads, int smem);
+
+// Chooses the SIMT kernel configuration. Parameters follow lbc_params
+// (include/lowbit_b200.h); zero fields take the defaults below.
+int plan_gemv(int fmt, int M, int N, int Kp, const lbc_params *p, GemvPlan &P) {
+  const DevInfo di = dev_info();
+  const int kgran = (fmt == lbc::FMT_MXFP4) ? 32 : 128;
+  const int MAXSEG = 1024 * 32;  // 256 threads x 4 chunks x 32 elements
+  const bool user_kb = p && p->kb > 0;
+
+  auto pick_threads = [&](int seg, int &tpr, int &ch) {
+    const int Cs = seg / 32;
+    ch = 1;
+    if (Cs <= 32) tpr = 32;
+    else if (Cs <= 64) tpr = 64;
+    else if (Cs <= 128) tpr = 128;
+    else if (Cs <= 256) tpr = 256;
+    else { tpr = 256; ch = Cs <= 512 ? 2 : 4; }
+  };
+  auto pick_mt = [&](int ch) {
+    int cap = (fmt == lbc::FMT_W4A8) ? (ch == 1 ? 8 : ch == 2 ? 4 : 2) : (ch == 1 ? 4 : ch == 2 ? 2 : 1);
+    int mt = 1;
+    while (mt < M && mt < cap) mt <<= 1;
+    return mt;
+  };
+
+  int seg = Kp;
+  if (user_kb) seg = std::min(Kp, round_up(p->kb, 128));
+  if (seg > MAXSEG) seg = MAXSEG;
+  int tpr, ch;
+  pick_threads(seg, tpr, ch);
+  int mt = (p && p->mr > 0) ? p->mr : pick_mt(ch);
+  int rt = (p && p->nr > 0) ? (p->nr >= 4 ? 4 : 1) : (mt <= 2 ? 4 : 1);
+  int nt = std::max(256, tpr);
+  int tile_rows = rt * (nt / tpr);
+  int passes = ceil_div(M, mt);
+
+  // split K when the row tiles alone cannot fill the GPU
+  if (!user_kb && seg == Kp && Kp >= 1024) {
+    const int work = ceil_div(N, tile_rows) * passes;
+    if (2 * work <= di.sms) {
+      int ns = std::min(std::min(ceil_div(di.sms, work), Kp / 512), 16);
+      if (ns > 1) {
+        seg = round_up(ceil_div(Kp, ns), 128);
+        pick_threads(seg, tpr, ch);
+        mt = (p && p->mr > 0) ? p->mr : pick_mt(ch);
+        rt = (p && p->nr > 0) ? (p->nr >= 4 ? 4 : 1) : (mt <= 2 ? 4 : 1);
+        nt = std::max(256, tpr);
+        tile_rows = rt * (nt / tpr);
+        passes = ceil_div(M, mt);
+      }
+    }
+  }
+  if (seg % kgran) return fail(LBC_ERR_PARAMS, "split-K length must be a multiple of 128");
+  if (!combo_ok(fmt, mt, ch, rt)) return fail(LBC_ERR_PARAMS, "tile (mr, nr) not compiled");
+
+  P.mt = mt; P.ch = ch; P.rt = rt; P.tpr = tpr; P.nt = nt; P.tile_rows = tile_rows;
+  P.seg = seg; P.nsplit = ceil_div(Kp, seg); P.passes = passes;
+  P.ntiles = ceil_div(N, tile_rows);
+  P.threads = nt + 32;
+
+  const int stage_bytes = tile_rows * (seg / 2);
+  int stages = (p && p->order > 0) ? p->order : std::min(16, std::max(2, ceil_div(65536, stage_bytes)));
+  if (stages > 32) stages = 32;
+  while (stages > 2 && lbc::gemv_smem_layout(stages, nt, tile_rows, seg / 2).total > di.smem_optin)
+    --stages;
+  const int smem = lbc::gemv_smem_layout(stages, nt, tile_rows, seg / 2).total;
+  if (smem > di.smem_optin) return fail(LBC_ERR_PARAMS, "tile does not fit in shared memory");
+  P.stages = stages;
+  P.smem = smem;
+
+  int cps = (p && p->nb > 0) ? p->nb : 2;
+  const int occ = occupancy(fmt, mt, ch, rt, P.threads, smem);
+  if (occ <= 0) return fail(LBC_ERR_PARAMS, "kernel configuration cannot be resident on an SM");
+  cps = std::min(cps, occ);
+  P.ctas_per_split = std::min(P.ntiles, std::max(1, di.sms * cps / P.nsplit));
+  return 0;
+}
+
+int occupancy_uncached(int fmt, int mt, int ch, int rt, int threads, int smem) {
+  switch (fmt) {
+    case lbc::FMT_W4A16: return lbc::gemv_occupancy<lbc::FMT_W4A16>(mt, ch, rt, threads, smem);
+    case lbc::FMT_MXFP4: return lbc::gemv_occupancy<lbc::FMT_MXFP4>(mt, ch, rt, threads, smem);
+    default: return lbc::gemv_occupancy<lbc::FMT_W4A8>(mt, ch, rt, threads, smem);
+  }
+}
+
+// occupancy results are cached per (device, kernel, block, smem): the planner
+// runs on every call and must not issue CUDA queries during graph capture
+int occupancy(int fmt, int mt, int ch, int rt, int threads, int smem) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  int d = 0;
+  cudaGetDevice(&d);
+  const uint64_t key = ((uint64_t)(d & 63) << 58) | ((uint64_t)(fmt & 3) << 56) |
+                       ((uint64_t)(mt & 15) << 52) | ((uint64_t)(ch & 7) << 49) |
+                       ((uint64_t)(rt & 7) << 46) | ((uint64_t)(threads & 2047) << 32) |
+                       (uint64_t)(uint32_t)smem;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int v = occupancy_uncached(fmt, mt, ch, rt, threads, smem);
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = v;
+  return v;
+}
+
+int run_gemv(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
+  GemvPlan P;
+  int rc = plan_gemv(fmt, a.M, a.N, a.Kp, p, P);
+  if (rc) return rc;
+  a.seg_elems = P.seg;
+  a.nsplit = P.nsplit;
+  a.ctas_per_split = P.ctas_per_split;
+  a.tile_rows = P.tile_rows;
+  a.ntiles = P.ntiles;
+  a.stages = P.stages;
+  a.tpr = P.tpr;
+  a.nt = P.nt;
+  a.atomic_out = P.nsplit > 1;
+  a.status = dev_info().status;
+  if (a.atomic_out) {
+    cudaError_t e = cudaMemsetAsync(a.y, 0, sizeof(float) * (size_t)a.M * a.N, st);
+    if (e != cudaSuccess) return fail_cuda("cudaMemsetAsync(y)", e);
+  }
+  const dim3 grid(P.nsplit * P.ctas_per_split, P.passes);
+  cudaError_t e;
+  switch (fmt) {
+    case lbc::FMT_W4A16: e = lbc::gemv_launch<lbc::FMT_W4A16>(a, P.mt, P.ch, P.rt, grid, P.threads, P.smem, st); break;
+    case lbc::FMT_MXFP4: e = lbc::gemv_launch<lbc::FMT_MXFP4>(a, P.mt, P.ch, P.rt, grid, P.threads, P.smem, st); break;
+    default: e = lbc::gemv_launch<lbc::FMT_W4A8>(a, P.mt, P.ch, P.rt, grid, P.threads, P.smem, st); break;
+  }
+  if (e != cudaSuccess) return fail_cuda("gemv launch", e);
+  return LBC_PATH_SIMT;
+}
+
+int device_gate() {
+  const DevInfo di = dev_info();
+  if (!di.ok) return fail(LBC_ERR_DEVICE, "current device is not an sm_100 GPU");
+  return 0;
+}
+
+size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum) {
+  const size_t xq_bytes = ((size_t)M * Kp + 255) / 256 * 256;
+  const size_t xs_bytes = ((size_t)M * 4 + 255) / 256 * 256;
+  const size_t as_bytes = ((size_t)M * (Kp / 128) * 4 + 255) / 256 * 256;
+  if (off_xs) *off_xs = xq_bytes;
+  if (off_asum) *off_asum = xq_bytes + xs_bytes;
+  return xq_bytes + xs_bytes + as_bytes;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int lbc_version(void) { return 1; }
+
+int lbc_device_ok(void) { return dev_info().ok; }
+
+int lbc_sm_count(void) { return dev_info().sms; }
+
+const char *lbc_last_error(void) { return g_err; }
+
+int lbc_device_status(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, lbc::g_status, sizeof(int)) != cudaSuccess) return LBC_ERR_CUDA;
+  if (reset && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(lbc::g_status, &z, sizeof(int));
+  }
+  return v;
+}
+
+int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
+                   const uint8_t *zeros, int N, float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
+  if (int rc = device_gate()) return rc;
+  lbc::GemvArgs a{};
+  a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+  a.M = M; a.N = N; a.Kp = Kp;
+  return run_gemv(lbc::FMT_W4A16, a, p, static_cast<cudaStream_t>(stream));
+}
+
+int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8_t *e8m0, int N,
+                   float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_MXBLOCK)) return rc;
+  if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
+  if (int rc = device_gate()) return rc;
+  lbc::GemvArgs a{};
+  a.x = x; a.qw = qw; a.e8m0 = e8m0; a.y = y;
+  a.M = M; a.N = N; a.Kp = Kp;
+  return run_gemv(lbc::FMT_MXFP4, a, p, static_cast<cudaStream_t>(stream));
+}
+
+int lbc_quant_act_int8(const float *x, int M, int Kp, int8_t *xq, float *xs, int32_t *asum,
+                       void *stream) {
+  if (int rc = check_shape(M, Kp, 1, LBC_GROUP)) return rc;
+  if (!x || !xq || !xs || !asum || !al16(x) || (reinterpret_cast<uintptr_t>(xq) & 3u))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer");
+  if (int rc = device_gate()) return rc;
+  cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda("quant_act_int8 launch", e);
+  return 0;
+}
+
+int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int M, int Kp,
+                    const uint8_t *qw, const float *scales, const uint8_t *zeros, int N, float *y,
+                    const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (!xq || !xs || !asum || !qw || !scales || !y || !al16(xq) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
+  if (int rc = device_gate()) return rc;
+  lbc::GemvArgs a{};
+  a.xq = xq; a.xs = xs; a.asum = asum; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+  a.M = M; a.N = N; a.Kp = Kp;
+  return run_gemv(lbc::FMT_W4A8, a, p, static_cast<cudaStream_t>(stream));
+}
+
+size_t lbc_gemm_w4a8_workspace_size(int M, int Kp) {
+  if (M <= 0 || Kp <= 0) return 0;
+  return w4a8_ws_layout(M, Kp, nullptr, nullptr);
+}
+
+int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
+                  const uint8_t *zeros, int N, float *y, const lbc_params *p, void *workspace,
+                  void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return fail(LBC_ERR_SHAPE, "workspace must be 256-byte aligned");
+  if (int rc = device_gate()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  size_t off_xs, off_as;
+  const size_t bytes = w4a8_ws_layout(M, Kp, &off_xs, &off_as);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  bool owned = false;
+  if (!ws) {
+    void *tmp = nullptr;
+    if (cudaMallocAsync(&tmp, bytes, st) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(LBC_ERR_ALLOC, "cudaMallocAsync(workspace) failed");
+    }
+    ws = static_cast<uint8_t *>(tmp);
+    owned = true;
+  }
+  int8_t *xq = reinterpret_cast<int8_t *>(ws);
+  float *xs = reinterpret_cast<float *>(ws + off_xs);
+  int32_t *asum = reinterpret_cast<int32_t *>(ws + off_as);
+  int rc = 0;
+  cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, st);
+  if (e != cudaSuccess) rc = fail_cuda("quant_act_int8 launch", e);
+  if (rc == 0) {
+    lbc::GemvArgs a{};
+    a.xq = xq; a.xs = xs; a.asum = asum; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+    a.M = M; a.N = N; a.Kp = Kp;
+    rc = run_gemv(lbc::FMT_W4A8, a, p, st);
+  }
+  if (owned) cudaFreeAsync(ws, st);
+  return rc;
+}
+
+int lbc_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, int Kp, const uint8_t *qw,
+                       const uint8_t *zeros, int N, int32_t *out, int isa, void *stream) {
+  (void)isa;
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (!xq || !asum || !qw || !out || !al16(xq) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
+  if (int rc = device_gate()) return rc;
+  cudaError_t e = lbc::launch_w4a8_group_acc(xq, asum, M, Kp, qw, zeros, N, out,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda("w4a8_group_acc launch", e);
+  return 0;
+}
+
+}  // extern "C"

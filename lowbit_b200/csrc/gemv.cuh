@@ -1,0 +1,440 @@
+// Decode-regime fused dequantize + GEMM on CUDA cores (any M; built for M <= 16).
+//
+// Arithmetic contract (the reference's scalar kernels, src/lowbit/csrc/
+// kern_scalar.c:10-74):
+//   W4A16 : y[m,n] = sum_g s[n,g] * sum_{k in g} (q[n,k] - z[n,g]) * x[m,k]     (fp32)
+//   MXFP4 : y[m,n] = sum_b 2^(e[n,b]-127) * sum_{k in b} e2m1(q[n,k]) * x[m,k]    (fp32)
+//   W4A8  : y[m,n] = xs[m] * sum_g s[n,g] * (sum_{k in g} q*xq - z*asum[m,g])  (int32 exact per
+//           16-byte chunk, fp32 across chunks)
+//
+// Structure (one persistent CTA per SM slot):
+//   * a producer warp streams weight tiles (tile_rows rows x one K segment)
+//     HBM -> shared memory with 1-D TMA bulk copies into a `stages`-deep ring
+//     guarded by full/empty mbarriers;
+//   * consumer threads own fixed 16-byte chunks of K: the activations of
+//     those chunks live in registers for the whole kernel, so shared memory
+//     only carries weights (1 byte per 2 MACs per token);
+//   * a "row team" of `tpr` threads covers one weight row; each thread keeps
+//     partial sums for RT rows x MT tokens, reduced with a transposing warp
+//     reduction and, for teams wider than a warp, one shared-memory step.
+//
+// Nibble decode without conversions: for a nibble at bit position p (0,4,8,12)
+// of a 16-bit half word, (w & (0xF << p)) | 0x4B000000 is the fp32 value
+// 2^23 + q*2^p; subtracting 2^23 + z*2^p gives (q - z)*2^p exactly. Four
+// accumulators (one per p) are rescaled by 2^-p at the end of each chunk.
+#pragma once
+
+#include "common.cuh"
+
+namespace lbc {
+
+enum : int { FMT_W4A16 = 0, FMT_MXFP4 = 1, FMT_W4A8 = 2 };
+
+struct GemvArgs {
+  const float *x;       // [M, Kp] fp32 (W4A16 / MXFP4)
+  const int8_t *xq;     // [M, Kp] int8 (W4A8)
+  const float *xs;      // [M]        (W4A8)
+  const int32_t *asum;  // [M, Kp/128] (W4A8) per-group code sums
+  const uint8_t *qw;    // [N, Kp/2]
+  const float *scales;  // [N, Kp/128] (int4)
+  const uint8_t *zeros; // [N, Kp/128] or nullptr (int4)
+  const uint8_t *e8m0;  // [N, Kp/32]  (MXFP4)
+  float *y;             // [M, N]
+  int M, N, Kp;
+  int seg_elems;        // K elements per split segment (multiple of 128)
+  int nsplit;           // number of K segments
+  int ctas_per_split;   // persistent CTAs working on one K segment
+  int tile_rows;        // rows per pipeline tile (= RT * teams)
+  int ntiles;           // ceil(N / tile_rows)
+  int stages;           // pipeline depth
+  int tpr;              // threads per row team (multiple of 32)
+  int nt;               // consumer threads (multiple of tpr)
+  int atomic_out;       // 1: accumulate into y with atomics (split-K)
+  int *status;          // device status word (bounded-wait timeouts)
+};
+
+// shared-memory carve-up; identical on host and device
+struct GemvSmem {
+  int bar_off, red_off, abort_off, stage_off, stage_bytes, total;
+};
+
+__host__ __device__ inline GemvSmem gemv_smem_layout(int stages, int nt, int tile_rows,
+                                                     int seg_bytes) {
+  GemvSmem L;
+  L.bar_off = 0;
+  L.red_off = 16 * stages;                    // full[S], empty[S] (8 B each)
+  L.abort_off = L.red_off + 2 * (nt / 32) * 32 * 4;
+  L.stage_off = (L.abort_off + 16 + 127) / 128 * 128;
+  L.stage_bytes = tile_rows * seg_bytes;
+  L.total = L.stage_off + stages * L.stage_bytes;
+  return L;
+}
+
+// ------------------------------------------------------------------ reductions
+// After the call, lane l holds in v[0] the warp-wide sum of value index
+// l / (32 / V) (all lanes of that group hold it). V must be a power of two <= 32.
+template <int V>
+__device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
+  constexpr int LOG2V = (V >= 32) ? 5 : (V >= 16) ? 4 : (V >= 8) ? 3 : (V >= 4) ? 2 : (V >= 2) ? 1 : 0;
+#pragma unroll
+  for (int st = 0; st < LOG2V; ++st) {
+    const int s = 16 >> st;
+    const int half = (V >> st) / 2;
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = up ? v[i] : v[i + half];
+      const float keep = up ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+#pragma unroll
+  for (int s = 16 >> LOG2V; s >= 1; s >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], s);
+  return v[0];
+}
+
+// ------------------------------------------------------------------ decoders
+// W4A16: one 16-byte chunk (32 codes of one group) against MT tokens.
+// xr[t][j] = (x[lo + j], x[hi + j]) with lo/hi the element bases of the chunk.
+template <int MT>
+__device__ __forceinline__ void dot_w4a16(const uint4 wv, uint32_t z, const float2 (*xr)[16],
+                                          float (&dot)[MT]) {
+  const uint32_t MAG = 0x4B000000u;
+  const float2 nz01 = make_float2(u2f(0xCB000000u | z), u2f(0xCB000000u | (z << 4)));
+  const float2 nz23 = make_float2(u2f(0xCB000000u | (z << 8)), u2f(0xCB000000u | (z << 12)));
+  float2 accA[MT], accB[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) accA[t] = accB[t] = make_float2(0.f, 0.f);
+  const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w = w4[q];
+    const uint32_t h = w >> 16;
+    float2 a = make_float2(u2f((w & 0x000Fu) | MAG), u2f((w & 0x00F0u) | MAG));
+    float2 b = make_float2(u2f((w & 0x0F00u) | MAG), u2f((w & 0xF000u) | MAG));
+    float2 c = make_float2(u2f((h & 0x000Fu) | MAG), u2f((h & 0x00F0u) | MAG));
+    float2 d = make_float2(u2f((h & 0x0F00u) | MAG), u2f((h & 0xF000u) | MAG));
+    a = __fadd2_rn(a, nz01);
+    b = __fadd2_rn(b, nz23);
+    c = __fadd2_rn(c, nz01);
+    d = __fadd2_rn(d, nz23);
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      accA[t] = __ffma2_rn(a, xr[t][4 * q + 0], accA[t]);
+      accB[t] = __ffma2_rn(b, xr[t][4 * q + 1], accB[t]);
+      accA[t] = __ffma2_rn(c, xr[t][4 * q + 2], accA[t]);
+      accB[t] = __ffma2_rn(d, xr[t][4 * q + 3], accB[t]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < MT; ++t)
+    dot[t] = fmaf(accB[t].y, 1.0f / 4096.0f,
+                  fmaf(accB[t].x, 1.0f / 256.0f, fmaf(accA[t].y, 1.0f / 16.0f, accA[t].x)));
+}
+
+// MXFP4: one 16-byte chunk = one block of 32 E2M1 codes. The result is
+// 2 * sum e2m1(q) * x (the caller's block scale carries the factor 1/2).
+// Codes are mapped through two 8-entry byte tables (prmt) to 16 + 2*e2m1(q),
+// a value in [4, 28], then to fp32 with the 2^23 magic number.
+template <int MT>
+__device__ __forceinline__ void dot_mxfp4(const uint4 wv, const float2 (*xr)[16], float (&dot)[MT]) {
+  const uint32_t TP0 = 0x13121110u, TP1 = 0x1C181614u;  // 16 + {0,1,2,3}, 16 + {4,6,8,12}
+  const uint32_t TN0 = 0x0D0E0F10u, TN1 = 0x04080A0Cu;  // 16 - {0,1,2,3}, 16 - {4,6,8,12}
+  const uint32_t MAGIC = 0x4B000000u;
+  const float2 NB = make_float2(-8388624.0f, -8388624.0f);  // -(2^23 + 16)
+  float2 accA[MT], accB[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) accA[t] = accB[t] = make_float2(0.f, 0.f);
+  const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w = w4[q];
+    const uint32_t m = w & 0x77777777u;
+    const uint32_t w4s = w << 4;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t sel = half ? (m >> 16) : m;
+      const uint32_t pos = prmt(TP0, TP1, sel);
+      const uint32_t neg = prmt(TN0, TN1, sel);
+      const uint32_t msk = prmt(w4s, w, half ? 0xFBEAu : 0xD9C8u);  // 0xFF where the code is negative
+      const uint32_t val = (pos & ~msk) | (neg & msk);               // bytes: 16 + 2*e2m1
+      float2 p0 = make_float2(u2f(prmt(val, MAGIC, 0x7540u)), u2f(prmt(val, MAGIC, 0x7541u)));
+      float2 p1 = make_float2(u2f(prmt(val, MAGIC, 0x7542u)), u2f(prmt(val, MAGIC, 0x7543u)));
+      p0 = __fadd2_rn(p0, NB);
+      p1 = __fadd2_rn(p1, NB);
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        accA[t] = __ffma2_rn(p0, xr[t][4 * q + 2 * half + 0], accA[t]);
+        accB[t] = __ffma2_rn(p1, xr[t][4 * q + 2 * half + 1], accB[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < MT; ++t) dot[t] = (accA[t].x + accA[t].y) + (accB[t].x + accB[t].y);
+}
+
+// 2^(e-128) as fp32: half the E8M0 block scale (the MXFP4 decoder returns 2x).
+// e == 255 is NaN, as in the OCP MX spec (src/lowbit/csrc/lowbit.h:84-88).
+__device__ __forceinline__ float e8m0_half_scale(uint32_t e) {
+  const uint32_t bits = (e == 255u) ? 0x7FC00000u : (e >= 2u ? (e - 1u) << 23 : (0x00200000u << e));
+  return u2f(bits);
+}
+
+// ------------------------------------------------------------------ kernel
+template <int FMT, int MT, int CH, int RT>
+__global__ void gemv_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int V = RT * MT;
+  static_assert(V <= 32 && (V & (V - 1)) == 0, "RT*MT must be a power of two <= 32");
+
+  const int S = a.stages;
+  const int ncw = a.nt >> 5;
+  const int split = blockIdx.x / a.ctas_per_split;
+  const int cta = blockIdx.x - split * a.ctas_per_split;
+  const int k0 = split * a.seg_elems;
+  const int k1 = min(a.Kp, k0 + a.seg_elems);
+  const int Cs = (k1 - k0) >> 5;  // 16-byte chunks per row segment
+  const int SB = Cs << 4;         // bytes per row segment
+  const GemvSmem L = gemv_smem_layout(S, a.nt, a.tile_rows, a.seg_elems / 2);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+  uint64_t *empty = full + S;
+  float *red = reinterpret_cast<float *>(smem + L.red_off);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L.abort_off);
+  uint8_t *stage_base = smem + L.stage_off;
+  const int tid = threadIdx.x;
+  const int m0 = blockIdx.y * MT;
+  const int row_bytes = a.Kp >> 1;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncw);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int my_tiles =
+      (cta < a.ntiles) ? (a.ntiles - cta + a.ctas_per_split - 1) / a.ctas_per_split : 0;
+
+  // ---------------------------------------------------------------- producer
+  if (tid >= a.nt) {
+    if (tid == a.nt) {
+      const uint64_t pol = policy_evict_first();
+      for (int i = 0; i < my_tiles; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (uint32_t)(i / S) & 1u;
+        if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u, a.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int r0 = (cta + i * a.ctas_per_split) * a.tile_rows;
+        const int rows = min(a.tile_rows, a.N - r0);
+        uint8_t *dst = stage_base + s * L.stage_bytes;
+        const uint8_t *src = a.qw + (size_t)r0 * row_bytes + (k0 >> 1);
+        mbar_expect_tx(&full[s], (uint32_t)(rows * SB));
+        if (a.nsplit == 1) {
+          bulk_g2s(dst, src, (uint32_t)(rows * SB), &full[s], pol);
+        } else {
+          for (int r = 0; r < rows; ++r)
+            bulk_g2s(dst + r * SB, src + (size_t)r * row_bytes, (uint32_t)SB, &full[s], pol);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- consumers
+  const int lane = tid & 31, warp = tid >> 5;
+  const int team = tid / a.tpr, tin = tid - team * a.tpr;
+  const int RP = a.nt / a.tpr;
+  const int G = a.Kp >> 7;        // int4 groups per row
+  const int NB32 = a.Kp >> 5;     // MXFP4 blocks per row
+
+  // activations of this thread's chunks, resident for the whole kernel
+  float2 xr[CH][MT][16];
+  uint32_t xl[CH][MT][4], xh[CH][MT][4];
+  int xsum[CH][MT];
+  (void)xr; (void)xl; (void)xh; (void)xsum;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = tin + i * a.tpr;
+    const int kc = (k0 >> 5) + c;  // global chunk index
+    int lo, hi;
+    if (FMT == FMT_MXFP4) {
+      lo = kc << 5;
+      hi = lo + 16;
+    } else {
+      lo = ((kc >> 2) << 7) + ((kc & 3) << 4);
+      hi = lo + 64;
+    }
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const int m = m0 + t;
+      const bool ok = (c < Cs) && (m < a.M);
+      if (FMT == FMT_W4A8) {
+        uint4 vl = make_uint4(0, 0, 0, 0), vh = make_uint4(0, 0, 0, 0);
+        if (ok) {
+          vl = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + lo));
+          vh = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + hi));
+        }
+        xl[i][t][0] = vl.x; xl[i][t][1] = vl.y; xl[i][t][2] = vl.z; xl[i][t][3] = vl.w;
+        xh[i][t][0] = vh.x; xh[i][t][1] = vh.y; xh[i][t][2] = vh.z; xh[i][t][3] = vh.w;
+        // z * asum[m,g] is subtracted once per group, in the group's first chunk,
+        // exactly as the reference applies it (src/lowbit/csrc/kern_scalar.c:49-59)
+        xsum[i][t] = (ok && (kc & 3) == 0) ? __ldg(a.asum + (size_t)m * (a.Kp >> 7) + (kc >> 2)) : 0;
+      } else {
+        const float4 *pl = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + lo);
+        const float4 *ph = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + hi);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f), h4 = l4;
+          if (ok) {
+            l4 = __ldg(pl + q);
+            h4 = __ldg(ph + q);
+          }
+          xr[i][t][4 * q + 0] = make_float2(l4.x, h4.x);
+          xr[i][t][4 * q + 1] = make_float2(l4.y, h4.y);
+          xr[i][t][4 * q + 2] = make_float2(l4.z, h4.z);
+          xr[i][t][4 * q + 3] = make_float2(l4.w, h4.w);
+        }
+      }
+    }
+  }
+
+  bool ok = true;
+  for (int it = 0; it < my_tiles; ++it) {
+    const int s = it % S;
+    const uint32_t ph = (uint32_t)(it / S) & 1u;
+    const int r0 = (cta + it * a.ctas_per_split) * a.tile_rows;
+    const int rows = min(a.tile_rows, a.N - r0);
+
+    // per-(row, chunk) scale and zero point, fetched before waiting on the tile
+    float sc[RT][CH];
+    uint32_t zz[RT][CH];
+#pragma unroll
+    for (int j = 0; j < RT; ++j) {
+      const int n = r0 + team + j * RP;
+      const bool rv = (team + j * RP) < rows;
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        const int c = tin + i * a.tpr;
+        const int kc = (k0 >> 5) + c;
+        sc[j][i] = 0.f;
+        zz[j][i] = 8u;
+        if (rv && c < Cs) {
+          if (FMT == FMT_MXFP4) {
+            sc[j][i] = e8m0_half_scale(__ldg(a.e8m0 + (size_t)n * NB32 + kc));
+          } else {
+            const size_t gi = (size_t)n * G + (kc >> 2);
+            sc[j][i] = __ldg(a.scales + gi);
+            if (a.zeros) zz[j][i] = __ldg(a.zeros + gi);
+          }
+        }
+      }
+    }
+
+    if (ok) ok = !(*abort_flag) && mbar_wait(&full[s], ph, a.status);
+    if (!ok) *abort_flag = 1;
+    const uint8_t *st = stage_base + s * L.stage_bytes;
+
+    float part[RT][MT];
+#pragma unroll
+    for (int j = 0; j < RT; ++j)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) part[j][t] = 0.f;
+
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        const int r = team + j * RP;
+        if (r < rows) {
+#pragma unroll
+          for (int i = 0; i < CH; ++i) {
+            const int c = tin + i * a.tpr;
+            if (c < Cs) {
+              const uint4 wv = lds128(st + r * SB + (c << 4));
+              if (FMT == FMT_W4A8) {
+                int acc[MT];
+#pragma unroll
+                for (int t = 0; t < MT; ++t) acc[t] = 0;
+                const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint32_t lo = w4[q] & 0x0F0F0F0Fu;
+                  const uint32_t hi = (w4[q] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                  for (int t = 0; t < MT; ++t) {
+                    acc[t] = dp4a_us(lo, xl[i][t][q], acc[t]);
+                    acc[t] = dp4a_us(hi, xh[i][t][q], acc[t]);
+                  }
+                }
+#pragma unroll
+                for (int t = 0; t < MT; ++t) {
+                  const int d = acc[t] - (int)zz[j][i] * xsum[i][t];
+                  part[j][t] = fmaf((float)d, sc[j][i], part[j][t]);
+                }
+              } else {
+                float dot[MT];
+                if (FMT == FMT_W4A16)
+                  dot_w4a16<MT>(wv, zz[j][i], xr[i], dot);
+                else
+                  dot_mxfp4<MT>(wv, xr[i], dot);
+#pragma unroll
+                for (int t = 0; t < MT; ++t) part[j][t] = fmaf(dot[t], sc[j][i], part[j][t]);
+              }
+            }
+          }
+        }
+      }
+    }
+    // release the stage (every consumer warp arrives once per tile)
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    // reduce RT x MT partials over the row team
+    float v[V];
+#pragma unroll
+    for (int j = 0; j < RT; ++j)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) v[j * MT + t] = part[j][t];
+    const float tot = warp_reduce_multi<V>(v, lane);
+    constexpr int PER = 32 / V;
+    int out_idx = -1;
+    float out_val = 0.f;
+    if (a.tpr == 32) {
+      if ((lane % PER) == 0) {
+        out_idx = lane / PER;
+        out_val = tot;
+      }
+    } else {
+      float *rb = red + (it & 1) * ncw * 32;
+      if ((lane % PER) == 0) rb[warp * 32 + lane / PER] = tot;
+      named_bar_sync(1, a.nt);
+      const int wpt = a.tpr >> 5;
+      if (tin < V) {
+        float acc = 0.f;
+        for (int w = 0; w < wpt; ++w) acc += rb[(team * wpt + w) * 32 + tin];
+        out_idx = tin;
+        out_val = acc;
+      }
+    }
+    if (ok && out_idx >= 0) {
+      const int j = out_idx / MT, t = out_idx - (out_idx / MT) * MT;
+      const int r = team + j * RP;
+      const int m = m0 + t;
+      if (r < rows && m < a.M) {
+        float val = out_val;
+        if (FMT == FMT_W4A8) val *= __ldg(a.xs + m);
+        float *dst = a.y + (size_t)m * a.N + (r0 + r);
+        if (a.atomic_out)
+          atomicAdd(dst, val);
+        else
+          *dst = val;
+      }
+    }
+  }
+}
+
+}  // namespace lbc

@@ -1,0 +1,16 @@
+// Internal launcher declarations (not part of the public C ABI).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lbc {
+
+cudaError_t launch_quant_act_int8(const float *x, int M, int Kp, int8_t *xq, float *xs,
+                                  int32_t *asum, cudaStream_t st);
+
+cudaError_t launch_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, int Kp,
+                                  const uint8_t *qw, const uint8_t *zeros, int N, int32_t *out,
+                                  cudaStream_t st);
+
+}  // namespace lbc

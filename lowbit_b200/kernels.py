@@ -1,0 +1,329 @@
+"""ctypes binding of liblowbit_b200.so: lowbit's kernel API on B200 GPUs.
+
+Mirrors src/lowbit/kernels.py (same function names, argument meaning and
+error behaviour) with the computation on the GPU:
+
+* ``x`` may be a numpy array (uploaded per call; the result comes back as a
+  numpy array, synchronously) or a torch CUDA tensor (no copies; the result is
+  a torch CUDA tensor produced on the current stream, no synchronisation);
+* weights may hold numpy arrays (uploaded once and cached on the object) or
+  torch CUDA tensors;
+* ``params`` is a :class:`Params` (fields reinterpreted for the GPU, see
+  include/lowbit_b200.h), ``None`` or ``"auto"`` (tuned cache, lowbit_b200.tune);
+* ``isa`` selects the kernel path: None/"auto" (M <= 16 SIMT fp32, larger M
+  the tensor-core path when available), "simt", "tcgen05"; the reference's CPU
+  ISA names ("scalar", "avx2", "avx512") are accepted and mean "auto";
+* ``threads`` is accepted and ignored (CPU thread count).
+
+A negative return code raises ValueError for shape/parameter errors (as the
+reference, src/lowbit/kernels.py:132-135) and RuntimeError for CUDA errors.
+There is no CPU fallback: without a CUDA device every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import asdict, dataclass
+from functools import lru_cache
+
+import numpy as np
+
+from ._build import build
+from .formats import GROUP, Int4Weights, Int8Acts, MXFP4Weights, pad_to
+
+PATHS = {-1: "auto", 0: "simt", 1: "tcgen05"}
+PATH_IDS = {"auto": -1, "simt": 0, "tcgen05": 1}
+REFERENCE_ISAS = ("scalar", "avx2", "avx512")
+KIND_IDS = {"w4a16": 0, "mxfp4": 1, "w4a8": 2}
+ERR_NAMES = {-1: "bad shape or pointer", -2: "tile parameters not supported", -3: "allocation failed",
+             -5: "CUDA error", -6: "device is not sm_100", -7: "device-side wait timed out"}
+
+
+class _Params(C.Structure):
+    _fields_ = [(f, C.c_int) for f in ("isa", "mr", "nr", "nb", "kb", "order", "nthreads")]
+
+
+@dataclass(frozen=True)
+class Params:
+    """Kernel tiling parameters (0 = library default), reinterpreted for the GPU:
+
+    mr    tokens per pass of the SIMT kernels (1, 2, 4, 8)
+    nr    rows per team per pipeline tile (1 or 4)
+    nb    resident CTAs per SM
+    kb    split-K length in elements (multiple of 128), 0 = whole K
+    order TMA pipeline stages
+    """
+    mr: int = 0
+    nr: int = 0
+    nb: int = 0
+    kb: int = 0
+    order: int = 0
+
+    def as_dict(self) -> dict:
+        return asdict(self)
+
+
+_vp = C.c_void_p
+_int = C.c_int
+_pp = C.POINTER(_Params)
+
+
+@lru_cache(maxsize=1)
+def lib() -> C.CDLL:
+    """Load (building first if needed) the CUDA library."""
+    import torch  # noqa: F401  (initialises the CUDA runtime torch uses)
+    so = C.CDLL(str(build()))
+    sig = {
+        "lbc_version": ([], _int),
+        "lbc_device_ok": ([], _int),
+        "lbc_sm_count": ([], _int),
+        "lbc_last_error": ([], C.c_char_p),
+        "lbc_device_status": ([_int], _int),
+        "lbc_gemm_w4a16": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
+        "lbc_gemm_mxfp4": ([_vp, _int, _int, _vp, _vp, _int, _vp, _pp, _vp], _int),
+        "lbc_gemm_w4a8_workspace_size": ([_int, _int], C.c_size_t),
+        "lbc_gemm_w4a8": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp, _vp], _int),
+        "lbc_gemm_w4a8_q": ([_vp, _vp, _vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
+        "lbc_quant_act_int8": ([_vp, _int, _int, _vp, _vp, _vp, _vp], _int),
+        "lbc_w4a8_group_acc": ([_vp, _vp, _int, _int, _vp, _vp, _int, _vp, _int, _vp], _int),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(so, name)
+        fn.argtypes = args
+        fn.restype = res
+    return so
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def gpu_info() -> dict:
+    torch = _torch()
+    from ._torch import require_cuda
+    require_cuda()
+    d = torch.cuda.current_device()
+    props = torch.cuda.get_device_properties(d)
+    L = lib()
+    return {"device": props.name, "index": d, "cc": f"{props.major}.{props.minor}",
+            "sm_count": L.lbc_sm_count(), "sm100": bool(L.lbc_device_ok()),
+            "lib_version": L.lbc_version(), "mem_gb": round(props.total_memory / 2**30, 1)}
+
+
+def cpu_info() -> dict:
+    """lowbit.cpu_info() compatibility: the keys callers read, describing the GPU backend."""
+    g = gpu_info()
+    return {"cpu_isa": "sm_100a", "active_isa": "sm_100a", "vnni": False, "openmp": False,
+            "max_threads": 1, "amx": False, "gpu": g}
+
+
+def _path_id(isa) -> int:
+    if isa is None or isa == "auto" or isa in REFERENCE_ISAS:
+        return -1
+    if isinstance(isa, int):
+        return isa if isa in PATHS else -1
+    if isa not in PATH_IDS:
+        raise ValueError(f"isa must be one of {sorted(PATH_IDS)} or a lowbit ISA name, not {isa!r}")
+    return PATH_IDS[isa]
+
+
+def effective_isa(kind: str, isa=None, m: int = 1) -> str:
+    """Kernel path a GEMM of `kind` with `m` tokens runs on."""
+    pid = _path_id(isa)
+    if pid == -1:
+        pid = 0
+    return PATHS[pid]
+
+
+_AUTO_MEMO: dict = {}
+
+
+def auto_params(kind: str, m: int, n: int, k: int, isa=None, threads=None) -> Params:
+    """Tuned parameters from the tune cache (lowbit_b200.tune), else defaults."""
+    key = (kind, m, n, k, isa)
+    if key not in _AUTO_MEMO:
+        from .tune import lookup
+        _AUTO_MEMO[key] = lookup(kind, m, n, k, isa) or Params()
+    return _AUTO_MEMO[key]
+
+
+def _params(p, isa, kind=None, shape=None) -> _Params:
+    if isinstance(p, str):
+        if p != "auto":
+            raise ValueError(f"params must be a Params, None or 'auto', not {p!r}")
+        p = auto_params(kind, *shape, isa=isa)
+    p = p or Params()
+    return _Params(_path_id(isa), p.mr, p.nr, p.nb, p.kb, p.order, 0)
+
+
+def _check(rc: int, what: str) -> int:
+    if rc < 0:
+        detail = lib().lbc_last_error().decode(errors="replace")
+        msg = f"{what} failed (rc={rc}, {ERR_NAMES.get(rc, 'error')}): {detail}"
+        if rc in (-1, -2):
+            raise ValueError(msg)
+        raise RuntimeError(msg)
+    return rc
+
+
+# ---------------------------------------------------------------- operands
+
+def _dev_weights(w):
+    """The weight container with its arrays on the current CUDA device (cached)."""
+    torch = _torch()
+    if isinstance(w.qw, torch.Tensor) and w.qw.is_cuda:
+        return w
+    cache = getattr(w, "_lbc_dev", None)
+    dev = torch.cuda.current_device()
+    if cache is None or cache[0] != dev:
+        cache = (dev, w.cuda())
+        object.__setattr__(w, "_lbc_dev", cache)
+    return cache[1]
+
+
+class _Prepared:
+    """Padded device X plus an output buffer, reusable across calls (timing reps)."""
+
+    def __init__(self, x, kp: int, n: int):
+        torch = _torch()
+        from ._torch import to_cuda
+        self.host = not isinstance(x, torch.Tensor)
+        if self.host:
+            x = np.asarray(x, np.float32)
+            if x.ndim == 1:
+                x = x[None]
+            xt = to_cuda(x)
+        else:
+            xt = x if x.dim() == 2 else x.reshape(1, -1)
+            if not xt.is_cuda:
+                xt = to_cuda(xt)
+            xt = xt.to(torch.float32)
+        if xt.shape[1] != kp:
+            if xt.shape[1] > kp:
+                raise ValueError(f"x has {xt.shape[1]} columns, more than Kp={kp}")
+            xt = torch.nn.functional.pad(xt, (0, kp - xt.shape[1]))
+        self.x = xt.contiguous()
+        self.m = int(self.x.shape[0])
+        self.y = torch.empty((self.m, n), dtype=torch.float32, device=self.x.device)
+
+    def result(self):
+        return self.y.cpu().numpy() if self.host else self.y
+
+
+def _call(fn_name, *args):
+    return getattr(lib(), fn_name)(*args)
+
+
+def _stream():
+    from ._torch import stream_handle
+    return stream_handle()
+
+
+# ---------------------------------------------------------------- GEMMs
+
+def gemm_w4a16(x, w: Int4Weights, params: Params | None = None, isa=None,
+               threads: int | None = None, _prep: _Prepared | None = None):
+    """Y = X @ dequant(W).T for int4 g128 weights (fp32 activations)."""
+    pr = _prep or _Prepared(x, w.kp, w.n)
+    d = _dev_weights(w)
+    rc = _call("lbc_gemm_w4a16", pr.x.data_ptr(), pr.m, w.kp, d.qw.data_ptr(), d.scales.data_ptr(),
+               None if d.zeros is None else d.zeros.data_ptr(), w.n, pr.y.data_ptr(),
+               C.byref(_params(params, isa, "w4a16", (pr.m, w.n, w.k))), _stream())
+    _check(rc, "lbc_gemm_w4a16")
+    return pr.result()
+
+
+def gemm_mxfp4(x, w: MXFP4Weights, params: Params | None = None, isa=None,
+               threads: int | None = None, _prep: _Prepared | None = None):
+    """Y = X @ dequant(W).T for OCP MXFP4 weights."""
+    pr = _prep or _Prepared(x, w.kp, w.n)
+    d = _dev_weights(w)
+    rc = _call("lbc_gemm_mxfp4", pr.x.data_ptr(), pr.m, w.kp, d.qw.data_ptr(), d.e8m0.data_ptr(), w.n,
+               pr.y.data_ptr(), C.byref(_params(params, isa, "mxfp4", (pr.m, w.n, w.k))), _stream())
+    _check(rc, "lbc_gemm_mxfp4")
+    return pr.result()
+
+
+_WS: dict = {}
+
+
+def _workspace(nbytes: int):
+    """Cached device scratch per (device, size class); stream-ordered reuse."""
+    torch = _torch()
+    dev = torch.cuda.current_device()
+    cur = _WS.get(dev)
+    if cur is None or cur.numel() < nbytes:
+        cur = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=dev)
+        _WS[dev] = cur
+    return cur
+
+
+def gemm_w4a8(x, w: Int4Weights, params: Params | None = None, isa=None,
+              threads: int | None = None, _prep: _Prepared | None = None):
+    """fp32 X in; X is quantized per token to int8 inside the call (counted in timings)."""
+    pr = _prep or _Prepared(x, w.kp, w.n)
+    d = _dev_weights(w)
+    ws = _workspace(int(lib().lbc_gemm_w4a8_workspace_size(pr.m, w.kp)))
+    rc = _call("lbc_gemm_w4a8", pr.x.data_ptr(), pr.m, w.kp, d.qw.data_ptr(), d.scales.data_ptr(),
+               None if d.zeros is None else d.zeros.data_ptr(), w.n, pr.y.data_ptr(),
+               C.byref(_params(params, isa, "w4a8", (pr.m, w.n, w.k))), ws.data_ptr(), _stream())
+    _check(rc, "lbc_gemm_w4a8")
+    return pr.result()
+
+
+def _dev_acts(a: Int8Acts):
+    from ._torch import to_cuda
+    torch = _torch()
+    host = not isinstance(a.xq, torch.Tensor)
+    return host, to_cuda(a.xq), to_cuda(a.scale), to_cuda(a.gsum)
+
+
+def gemm_w4a8_q(a: Int8Acts, w: Int4Weights, params: Params | None = None, isa=None,
+                threads: int | None = None):
+    """W4A8 GEMM on already-quantized activations."""
+    torch = _torch()
+    host, xq, xs, gs = _dev_acts(a)
+    m = int(xq.shape[0])
+    d = _dev_weights(w)
+    y = torch.empty((m, w.n), dtype=torch.float32, device=xq.device)
+    rc = _call("lbc_gemm_w4a8_q", xq.data_ptr(), xs.data_ptr(), gs.data_ptr(), m, w.kp, d.qw.data_ptr(),
+               d.scales.data_ptr(), None if d.zeros is None else d.zeros.data_ptr(), w.n, y.data_ptr(),
+               C.byref(_params(params, isa, "w4a8", (m, w.n, w.k))), _stream())
+    _check(rc, "lbc_gemm_w4a8_q")
+    return y.cpu().numpy() if host else y
+
+
+def quant_act_int8(x, kp: int) -> Int8Acts:
+    """Per-token int8 quantization on the GPU (bit-identical to formats.quantize_act_int8)."""
+    torch = _torch()
+    pr = _Prepared(np.atleast_2d(x) if not isinstance(x, torch.Tensor) else x, kp, 1)
+    m = pr.m
+    xq = torch.empty((m, kp), dtype=torch.int8, device=pr.x.device)
+    xs = torch.empty((m,), dtype=torch.float32, device=pr.x.device)
+    gs = torch.empty((m, kp // GROUP), dtype=torch.int32, device=pr.x.device)
+    _check(_call("lbc_quant_act_int8", pr.x.data_ptr(), m, kp, xq.data_ptr(), xs.data_ptr(),
+                 gs.data_ptr(), _stream()), "lbc_quant_act_int8")
+    if pr.host:
+        return Int8Acts(xq.cpu().numpy(), xs.cpu().numpy(), gs.cpu().numpy())
+    return Int8Acts(xq, xs, gs)
+
+
+def w4a8_group_acc(a: Int8Acts, w: Int4Weights, isa=None):
+    """Exact int32 accumulators out[m, n, g] = sum_{k in g} (q - z) * xq (debug/test)."""
+    torch = _torch()
+    host, xq, _, gs = _dev_acts(a)
+    m = int(xq.shape[0])
+    d = _dev_weights(w)
+    out = torch.empty((m, w.n, w.kp // GROUP), dtype=torch.int32, device=xq.device)
+    _check(_call("lbc_w4a8_group_acc", xq.data_ptr(), gs.data_ptr(), m, w.kp, d.qw.data_ptr(),
+                 None if d.zeros is None else d.zeros.data_ptr(), w.n, out.data_ptr(), -1, _stream()),
+           "lbc_w4a8_group_acc")
+    return out.cpu().numpy() if host else out
+
+
+def device_status(reset: bool = True) -> int:
+    """0, or the error code a bounded device-side wait recorded (synchronous)."""
+    return int(lib().lbc_device_status(1 if reset else 0))
+
+
+GEMMS = {"w4a16": gemm_w4a16, "mxfp4": gemm_mxfp4, "w4a8": gemm_w4a8}
