@@ -89,6 +89,13 @@ const char *lbc_last_error(void);
  * bounded device-side wait gave up; reset != 0 clears it. Synchronous. */
 int lbc_device_status(int reset);
 
+/* Kernel configuration the planner picks for a GEMM of `kind` (0 w4a16,
+ * 1 mxfp4, 2 w4a8) as a JSON object in buf; returns the path or an error.
+ * Introspection for tuning; no reference counterpart (the reference's
+ * tiling driver, src/lowbit/csrc/dispatch.c:148-203, exposes none). */
+int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char *buf,
+                      int buflen);
+
 /* ---- GEMMs ---- */
 
 /* W4A16: replaces lb_gemm_w4a16 (src/lowbit/csrc/lowbit.h:104-106,

@@ -18,6 +18,10 @@ __global__ void quant_act_int8_kernel(const float *__restrict__ x, int Kp,
                                       int8_t *__restrict__ xq, float *__restrict__ xs,
                                       int32_t *__restrict__ asum) {
   __shared__ float wmax[32];
+  // let the GEMM that consumes xq start streaming its weights now; x may be
+  // produced by the previous kernel, so wait for it before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int m = blockIdx.x;
   const float *xr = x + (size_t)m * Kp;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -106,10 +110,16 @@ __global__ void w4a8_group_acc_kernel(const int8_t *__restrict__ xq,
 
 cudaError_t launch_quant_act_int8(const float *x, int M, int Kp, int8_t *xq, float *xs,
                                   int32_t *asum, cudaStream_t st) {
-  int threads = 256;
-  if (Kp <= 512) threads = 128;
-  quant_act_int8_kernel<<<M, threads, 0, st>>>(x, Kp, xq, xs, asum);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M, 1, 1);
+  cfg.blockDim = dim3(Kp <= 512 ? 128 : 256, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, quant_act_int8_kernel, x, Kp, xq, xs, asum);
 }
 
 cudaError_t launch_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, int Kp,

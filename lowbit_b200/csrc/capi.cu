@@ -72,8 +72,8 @@ int check_shape(int M, int Kp, int N, int block) {
 // ------------------------------------------------------------------ planner
 struct GemvPlan {
   int mt = 1, ch = 1, rt = 4, tpr = 32, nt = 256, tile_rows = 4, stages = 4;
-  int nsplit = 1, seg = 0, ctas_per_split = 1, ntiles = 1, passes = 1;
-  int threads = 288, smem = 0;
+  int nsplit = 1, seg = 0, ctas_per_split = 1, ntiles = 1, passes = 1, meta_tma = 0;
+  int threads = 256, smem = 0;
 };
 
 bool combo_ok(int fmt, int mt, int ch, int rt) {
@@ -94,7 +94,8 @@ int occupancy(int fmt, int mt, int ch, int rt, int threads, int smem);
 
 // Chooses the SIMT kernel configuration. Parameters follow lbc_params
 // (include/lowbit_b200.h); zero fields take the defaults below.
-int plan_gemv(int fmt, int M, int N, int Kp, const lbc_params *p, GemvPlan &P) {
+int plan_gemv(int fmt, int M, int N, int Kp, const lbc_params *p, GemvPlan &P, bool meta_ptrs_aligned,
+              bool has_zeros) {
   const DevInfo di = dev_info();
   const int kgran = (fmt == lbc::FMT_MXFP4) ? 32 : 128;
   const int MAXSEG = 1024 * 32;  // 256 threads x 4 chunks x 32 elements
@@ -123,7 +124,7 @@ int plan_gemv(int fmt, int M, int N, int Kp, const lbc_params *p, GemvPlan &P) {
   pick_threads(seg, tpr, ch);
   int mt = (p && p->mr > 0) ? p->mr : pick_mt(ch);
   int rt = (p && p->nr > 0) ? (p->nr >= 4 ? 4 : 1) : (mt <= 2 ? 4 : 1);
-  int nt = std::max(256, tpr);
+  const int nt = 256;  // consumer threads = CTA size (tpr <= 256)
   int tile_rows = rt * (nt / tpr);
   int passes = ceil_div(M, mt);
 
@@ -137,7 +138,6 @@ int plan_gemv(int fmt, int M, int N, int Kp, const lbc_params *p, GemvPlan &P) {
         pick_threads(seg, tpr, ch);
         mt = (p && p->mr > 0) ? p->mr : pick_mt(ch);
         rt = (p && p->nr > 0) ? (p->nr >= 4 ? 4 : 1) : (mt <= 2 ? 4 : 1);
-        nt = std::max(256, tpr);
         tile_rows = rt * (nt / tpr);
         passes = ceil_div(M, mt);
       }
@@ -149,21 +149,33 @@ int plan_gemv(int fmt, int M, int N, int Kp, const lbc_params *p, GemvPlan &P) {
   P.mt = mt; P.ch = ch; P.rt = rt; P.tpr = tpr; P.nt = nt; P.tile_rows = tile_rows;
   P.seg = seg; P.nsplit = ceil_div(Kp, seg); P.passes = passes;
   P.ntiles = ceil_div(N, tile_rows);
-  P.threads = nt + 32;
+  P.threads = nt;
 
-  const int stage_bytes = tile_rows * (seg / 2);
+  // scales / zero points / e8m0 ride in the stage when every tile's slice of
+  // them is a 16-byte aligned contiguous block (whole-K segments only)
+  {
+    const lbc::GemvMeta mm = lbc::gemv_meta(fmt, Kp, has_zeros, tile_rows, seg / 2, true);
+    P.meta_tma = (P.nsplit == 1) && meta_ptrs_aligned && ((tile_rows * mm.sc_row) % 16 == 0) &&
+                 ((tile_rows * mm.z_row) % 16 == 0);
+  }
+  const int stage_bytes = lbc::gemv_meta(fmt, Kp, has_zeros, tile_rows, seg / 2, P.meta_tma).bytes;
   int stages = (p && p->order > 0) ? p->order : std::min(16, std::max(2, ceil_div(65536, stage_bytes)));
   if (stages > 32) stages = 32;
-  while (stages > 2 && lbc::gemv_smem_layout(stages, nt, tile_rows, seg / 2).total > di.smem_optin)
-    --stages;
-  const int smem = lbc::gemv_smem_layout(stages, nt, tile_rows, seg / 2).total;
+  while (stages > 2 && lbc::gemv_smem_layout(stages, nt, stage_bytes).total > di.smem_optin) --stages;
+  const int smem = lbc::gemv_smem_layout(stages, nt, stage_bytes).total;
   if (smem > di.smem_optin) return fail(LBC_ERR_PARAMS, "tile does not fit in shared memory");
   P.stages = stages;
   P.smem = smem;
 
   int cps = (p && p->nb > 0) ? p->nb : 2;
   const int occ = occupancy(fmt, mt, ch, rt, P.threads, smem);
-  if (occ <= 0) return fail(LBC_ERR_PARAMS, "kernel configuration cannot be resident on an SM");
+  if (occ <= 0) {
+    snprintf(g_err, sizeof g_err,
+             "kernel configuration cannot be resident on an SM (fmt=%d mt=%d ch=%d rt=%d threads=%d "
+             "smem=%d: %s %s)", fmt, mt, ch, rt, P.threads, smem,
+             occ < 0 ? cudaGetErrorString((cudaError_t)(-occ)) : "occupancy 0", lbc::occ_note());
+    return LBC_ERR_PARAMS;
+  }
   cps = std::min(cps, occ);
   P.ctas_per_split = std::min(P.ntiles, std::max(1, di.sms * cps / P.nsplit));
   return 0;
@@ -199,9 +211,14 @@ int occupancy(int fmt, int mt, int ch, int rt, int threads, int smem) {
   return v;
 }
 
+bool meta_aligned(int fmt, const lbc::GemvArgs &a) {
+  if (fmt == lbc::FMT_MXFP4) return al16(a.e8m0);
+  return al16(a.scales) && (a.zeros == nullptr || al16(a.zeros));
+}
+
 int run_gemv(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
   GemvPlan P;
-  int rc = plan_gemv(fmt, a.M, a.N, a.Kp, p, P);
+  int rc = plan_gemv(fmt, a.M, a.N, a.Kp, p, P, meta_aligned(fmt, a), a.zeros != nullptr);
   if (rc) return rc;
   a.seg_elems = P.seg;
   a.nsplit = P.nsplit;
@@ -212,6 +229,7 @@ int run_gemv(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
   a.tpr = P.tpr;
   a.nt = P.nt;
   a.atomic_out = P.nsplit > 1;
+  a.meta_tma = P.meta_tma;
   a.status = dev_info().status;
   if (a.atomic_out) {
     cudaError_t e = cudaMemsetAsync(a.y, 0, sizeof(float) * (size_t)a.M * a.N, st);
@@ -264,6 +282,24 @@ int lbc_device_status(int reset) {
     cudaMemcpyToSymbol(lbc::g_status, &z, sizeof(int));
   }
   return v;
+}
+
+int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char *buf, int buflen) {
+  if (kind < 0 || kind > 2) return fail(LBC_ERR_SHAPE, "kind must be 0 (w4a16), 1 (mxfp4) or 2 (w4a8)");
+  if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
+  if (int rc = device_gate()) return rc;
+  GemvPlan P;
+  const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
+  const int rc = plan_gemv(fmt, M, N, Kp, p, P, true, kind != 1);
+  if (rc) return rc;
+  if (buf && buflen > 0)
+    snprintf(buf, (size_t)buflen,
+             "{\"path\": \"simt\", \"mt\": %d, \"ch\": %d, \"rt\": %d, \"tpr\": %d, \"nt\": %d, "
+             "\"tile_rows\": %d, \"stages\": %d, \"nsplit\": %d, \"seg\": %d, \"ctas_per_split\": %d, "
+             "\"ntiles\": %d, \"passes\": %d, \"threads\": %d, \"smem\": %d, \"meta_tma\": %d}",
+             P.mt, P.ch, P.rt, P.tpr, P.nt, P.tile_rows, P.stages, P.nsplit, P.seg, P.ctas_per_split,
+             P.ntiles, P.passes, P.threads, P.smem, P.meta_tma);
+  return LBC_PATH_SIMT;
 }
 
 int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,

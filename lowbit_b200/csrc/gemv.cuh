@@ -7,10 +7,12 @@
 //   W4A8  : y[m,n] = xs[m] * sum_g s[n,g] * (sum_{k in g} q*xq - z*asum[m,g])  (int32 exact per
 //           16-byte chunk, fp32 across chunks)
 //
-// Structure (one persistent CTA per SM slot):
-//   * a producer warp streams weight tiles (tile_rows rows x one K segment)
-//     HBM -> shared memory with 1-D TMA bulk copies into a `stages`-deep ring
-//     guarded by full/empty mbarriers;
+// Structure (persistent CTAs of 8 warps, 1-3 per SM):
+//   * weight tiles (tile_rows rows x one K segment) stream HBM -> shared memory
+//     as 1-D TMA bulk copies into a `stages`-deep ring guarded by full/empty
+//     mbarriers; thread 0 issues the copies (no dedicated producer warp: B200
+//     splits the register file over 4 SM sub-partitions, and a 9th warp would
+//     cap every thread at 168 registers);
 //   * consumer threads own fixed 16-byte chunks of K: the activations of
 //     those chunks live in registers for the whole kernel, so shared memory
 //     only carries weights (1 byte per 2 MACs per token);
@@ -50,24 +52,58 @@ struct GemvArgs {
   int tpr;              // threads per row team (multiple of 32)
   int nt;               // consumer threads (multiple of tpr)
   int atomic_out;       // 1: accumulate into y with atomics (split-K)
+  int meta_tma;         // 1: scales/zeros/e8m0 travel with the weights in each stage
   int *status;          // device status word (bounded-wait timeouts)
 };
+
+// Per-stage metadata region (scales + zero points, or E8M0 exponents) when it
+// is staged by TMA: bytes per row of each part, rounded regions per stage.
+struct GemvMeta {
+  int sc_row;   // bytes of scales (int4: G*4) or e8m0 (MXFP4: Kp/32) per row
+  int z_row;    // bytes of zero points per row (0 when absent / MXFP4)
+  int sc_off;   // offset of the scale region inside a stage
+  int z_off;    // offset of the zero-point region inside a stage
+  int bytes;    // total stage bytes (weights + metadata)
+};
+
+__host__ __device__ inline int round16(int v) { return (v + 15) & ~15; }
+
+__host__ __device__ inline GemvMeta gemv_meta(int fmt, int Kp, bool has_zeros, int tile_rows,
+                                              int seg_bytes, bool meta_tma) {
+  GemvMeta m;
+  m.sc_row = (fmt == 1) ? (Kp >> 5) : (Kp >> 7) * 4;
+  m.z_row = (fmt != 1 && has_zeros) ? (Kp >> 7) : 0;
+  m.sc_off = tile_rows * seg_bytes;
+  m.z_off = m.sc_off + (meta_tma ? round16(tile_rows * m.sc_row) : 0);
+  m.bytes = m.z_off + (meta_tma ? round16(tile_rows * m.z_row) : 0);
+  return m;
+}
 
 // shared-memory carve-up; identical on host and device
 struct GemvSmem {
   int bar_off, red_off, abort_off, stage_off, stage_bytes, total;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(int stages, int nt, int tile_rows,
-                                                     int seg_bytes) {
+__host__ __device__ inline GemvSmem gemv_smem_layout(int stages, int nt, int stage_bytes) {
   GemvSmem L;
   L.bar_off = 0;
-  L.red_off = 16 * stages;                    // full[S], empty[S] (8 B each)
+  L.red_off = 16 * stages;  // full[S], empty[S] (8 B each)
   L.abort_off = L.red_off + 2 * (nt / 32) * 32 * 4;
   L.stage_off = (L.abort_off + 16 + 127) / 128 * 128;
-  L.stage_bytes = tile_rows * seg_bytes;
+  L.stage_bytes = (stage_bytes + 127) / 128 * 128;
   L.total = L.stage_off + stages * L.stage_bytes;
   return L;
+}
+
+// ---------------------------------------------------------------- PDL hooks
+// Programmatic dependent launch: the next kernel in the stream may start once
+// every CTA of this one has called launch_dependents; it must call
+// wait_prior_grid before touching memory the previous kernel writes.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prior_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ reductions
@@ -182,7 +218,7 @@ __device__ __forceinline__ float e8m0_half_scale(uint32_t e) {
 
 // ------------------------------------------------------------------ kernel
 template <int FMT, int MT, int CH, int RT>
-__global__ void gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int V = RT * MT;
   static_assert(V <= 32 && (V & (V - 1)) == 0, "RT*MT must be a power of two <= 32");
@@ -195,7 +231,9 @@ __global__ void gemv_kernel(const GemvArgs a) {
   const int k1 = min(a.Kp, k0 + a.seg_elems);
   const int Cs = (k1 - k0) >> 5;  // 16-byte chunks per row segment
   const int SB = Cs << 4;         // bytes per row segment
-  const GemvSmem L = gemv_smem_layout(S, a.nt, a.tile_rows, a.seg_elems / 2);
+  const bool has_z = (FMT != FMT_MXFP4) && a.zeros != nullptr;
+  const GemvMeta MM = gemv_meta(FMT, a.Kp, has_z, a.tile_rows, a.seg_elems / 2, a.meta_tma != 0);
+  const GemvSmem L = gemv_smem_layout(S, a.nt, MM.bytes);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
   uint64_t *empty = full + S;
   float *red = reinterpret_cast<float *>(smem + L.red_off);
@@ -204,6 +242,8 @@ __global__ void gemv_kernel(const GemvArgs a) {
   const int tid = threadIdx.x;
   const int m0 = blockIdx.y * MT;
   const int row_bytes = a.Kp >> 1;
+  const int G = a.Kp >> 7;     // int4 groups per row
+  const int NB32 = a.Kp >> 5;  // MXFP4 blocks per row
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -218,41 +258,54 @@ __global__ void gemv_kernel(const GemvArgs a) {
   const int my_tiles =
       (cta < a.ntiles) ? (a.ntiles - cta + a.ctas_per_split - 1) / a.ctas_per_split : 0;
 
-  // ---------------------------------------------------------------- producer
-  if (tid >= a.nt) {
-    if (tid == a.nt) {
-      const uint64_t pol = policy_evict_first();
-      for (int i = 0; i < my_tiles; ++i) {
-        const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
-        if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u, a.status)) {
-          *abort_flag = 1;
-          break;
-        }
-        const int r0 = (cta + i * a.ctas_per_split) * a.tile_rows;
-        const int rows = min(a.tile_rows, a.N - r0);
-        uint8_t *dst = stage_base + s * L.stage_bytes;
-        const uint8_t *src = a.qw + (size_t)r0 * row_bytes + (k0 >> 1);
-        mbar_expect_tx(&full[s], (uint32_t)(rows * SB));
-        if (a.nsplit == 1) {
-          bulk_g2s(dst, src, (uint32_t)(rows * SB), &full[s], pol);
-        } else {
-          for (int r = 0; r < rows; ++r)
-            bulk_g2s(dst + r * SB, src + (size_t)r * row_bytes, (uint32_t)SB, &full[s], pol);
-        }
-      }
-    }
-    return;
-  }
+  // whether tile i's metadata is staged by TMA (the tail tile may be unaligned)
+  auto tile_meta = [&](int rows) -> bool {
+    if (!a.meta_tma) return false;
+    if (rows == a.tile_rows) return true;
+    return ((rows * MM.sc_row) & 15) == 0 && ((rows * MM.z_row) & 15) == 0;
+  };
 
-  // ---------------------------------------------------------------- consumers
+  // Thread 0 doubles as the TMA producer: it fills the first `stages` tiles
+  // up front, then refills the stage of tile i-1 with tile i-1+stages at the
+  // top of iteration i, once every warp has released tile i-1. No warp is
+  // dedicated to producing, so a CTA is exactly `nt` threads (8 warps) and
+  // every warp may use up to 255 registers.
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](int i) {
+    const int s = i % S;
+    const int r0 = (cta + i * a.ctas_per_split) * a.tile_rows;
+    const int rows = min(a.tile_rows, a.N - r0);
+    uint8_t *dst = stage_base + s * L.stage_bytes;
+    const uint8_t *src = a.qw + (size_t)r0 * row_bytes + (k0 >> 1);
+    const bool tm = tile_meta(rows);
+    const uint32_t mbytes = tm ? (uint32_t)(rows * (MM.sc_row + MM.z_row)) : 0u;
+    mbar_expect_tx(&full[s], (uint32_t)(rows * SB) + mbytes);
+    if (a.nsplit == 1) {
+      bulk_g2s(dst, src, (uint32_t)(rows * SB), &full[s], pol);
+    } else {
+      for (int r = 0; r < rows; ++r)
+        bulk_g2s(dst + r * SB, src + (size_t)r * row_bytes, (uint32_t)SB, &full[s], pol);
+    }
+    if (tm) {
+      const uint8_t *msrc = (FMT == FMT_MXFP4) ? a.e8m0 : reinterpret_cast<const uint8_t *>(a.scales);
+      bulk_g2s(dst + MM.sc_off, msrc + (size_t)r0 * MM.sc_row, (uint32_t)(rows * MM.sc_row), &full[s], pol);
+      if (MM.z_row)
+        bulk_g2s(dst + MM.z_off, a.zeros + (size_t)r0 * MM.z_row, (uint32_t)(rows * MM.z_row), &full[s], pol);
+    }
+  };
+  // weights and their metadata are static: stream them before the previous
+  // kernel in the stream (which may produce X) has finished
+  if (tid == 0)
+    for (int i = 0; i < min(S, my_tiles); ++i) issue(i);
+  pdl_launch_dependents();
+
   const int lane = tid & 31, warp = tid >> 5;
   const int team = tid / a.tpr, tin = tid - team * a.tpr;
   const int RP = a.nt / a.tpr;
-  const int G = a.Kp >> 7;        // int4 groups per row
-  const int NB32 = a.Kp >> 5;     // MXFP4 blocks per row
 
-  // activations of this thread's chunks, resident for the whole kernel
+  // activations (written by the previous kernel, if any) of this thread's
+  // chunks, resident in registers for the whole kernel
+  pdl_wait_prior_grid();
   float2 xr[CH][MT][16];
   uint32_t xl[CH][MT][4], xh[CH][MT][4];
   int xsum[CH][MT];
@@ -283,7 +336,7 @@ __global__ void gemv_kernel(const GemvArgs a) {
         xh[i][t][0] = vh.x; xh[i][t][1] = vh.y; xh[i][t][2] = vh.z; xh[i][t][3] = vh.w;
         // z * asum[m,g] is subtracted once per group, in the group's first chunk,
         // exactly as the reference applies it (src/lowbit/csrc/kern_scalar.c:49-59)
-        xsum[i][t] = (ok && (kc & 3) == 0) ? __ldg(a.asum + (size_t)m * (a.Kp >> 7) + (kc >> 2)) : 0;
+        xsum[i][t] = (ok && (kc & 3) == 0) ? __ldg(a.asum + (size_t)m * G + (kc >> 2)) : 0;
       } else {
         const float4 *pl = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + lo);
         const float4 *ph = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + hi);
@@ -307,37 +360,60 @@ __global__ void gemv_kernel(const GemvArgs a) {
   for (int it = 0; it < my_tiles; ++it) {
     const int s = it % S;
     const uint32_t ph = (uint32_t)(it / S) & 1u;
+    // refill the stage released by tile it-1 with tile it-1+S
+    if (tid == 0 && it >= 1 && it - 1 + S < my_tiles) {
+      const int sp = (it - 1) % S;
+      const uint32_t php = (uint32_t)((it - 1) / S) & 1u;
+      if (ok) ok = !(*abort_flag) && mbar_wait(&empty[sp], php, a.status);
+      if (ok)
+        issue(it - 1 + S);
+      else
+        *abort_flag = 1;
+    }
     const int r0 = (cta + it * a.ctas_per_split) * a.tile_rows;
     const int rows = min(a.tile_rows, a.N - r0);
+    const bool tm = tile_meta(rows);
+    const uint8_t *st = stage_base + s * L.stage_bytes;
 
-    // per-(row, chunk) scale and zero point, fetched before waiting on the tile
+    // per-(row, chunk) scale and zero point: from the stage when TMA brought
+    // them, else fetched from global memory before waiting on the tile
     float sc[RT][CH];
     uint32_t zz[RT][CH];
+    auto fetch_meta = [&](bool from_smem) {
 #pragma unroll
-    for (int j = 0; j < RT; ++j) {
-      const int n = r0 + team + j * RP;
-      const bool rv = (team + j * RP) < rows;
+      for (int j = 0; j < RT; ++j) {
+        const int r = team + j * RP;
+        const int n = r0 + r;
+        const bool rv = r < rows;
 #pragma unroll
-      for (int i = 0; i < CH; ++i) {
-        const int c = tin + i * a.tpr;
-        const int kc = (k0 >> 5) + c;
-        sc[j][i] = 0.f;
-        zz[j][i] = 8u;
-        if (rv && c < Cs) {
-          if (FMT == FMT_MXFP4) {
-            sc[j][i] = e8m0_half_scale(__ldg(a.e8m0 + (size_t)n * NB32 + kc));
-          } else {
-            const size_t gi = (size_t)n * G + (kc >> 2);
-            sc[j][i] = __ldg(a.scales + gi);
-            if (a.zeros) zz[j][i] = __ldg(a.zeros + gi);
+        for (int i = 0; i < CH; ++i) {
+          const int c = tin + i * a.tpr;
+          const int kc = (k0 >> 5) + c;
+          sc[j][i] = 0.f;
+          zz[j][i] = 8u;
+          if (rv && c < Cs) {
+            if (FMT == FMT_MXFP4) {
+              const uint32_t e = from_smem ? st[MM.sc_off + r * NB32 + kc] : __ldg(a.e8m0 + (size_t)n * NB32 + kc);
+              sc[j][i] = e8m0_half_scale(e);
+            } else {
+              const int g = kc >> 2;
+              if (from_smem) {
+                sc[j][i] = reinterpret_cast<const float *>(st + MM.sc_off)[r * G + g];
+                if (has_z) zz[j][i] = st[MM.z_off + r * G + g];
+              } else {
+                sc[j][i] = __ldg(a.scales + (size_t)n * G + g);
+                if (has_z) zz[j][i] = __ldg(a.zeros + (size_t)n * G + g);
+              }
+            }
           }
         }
       }
-    }
+    };
+    if (!tm) fetch_meta(false);
 
     if (ok) ok = !(*abort_flag) && mbar_wait(&full[s], ph, a.status);
     if (!ok) *abort_flag = 1;
-    const uint8_t *st = stage_base + s * L.stage_bytes;
+    if (tm) fetch_meta(true);
 
     float part[RT][MT];
 #pragma unroll

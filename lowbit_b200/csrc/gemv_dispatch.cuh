@@ -4,6 +4,7 @@
 #pragma once
 
 #include <atomic>
+#include <cstdio>
 
 #include "gemv.cuh"
 
@@ -19,6 +20,12 @@ cudaError_t gemv_launch(const GemvArgs &a, int mt, int ch, int rt, dim3 grid, in
 // shared memory (0 when not instantiated or not launchable).
 template <int FMT>
 int gemv_occupancy(int mt, int ch, int rt, int threads, int smem);
+
+// thread-local note describing the last zero-occupancy configuration
+inline char *occ_note() {
+  static thread_local char buf[160] = "";
+  return buf;
+}
 
 namespace detail {
 // Largest dynamic shared memory size already enabled for this instantiation on
@@ -41,24 +48,45 @@ cudaError_t ensure_smem(int smem) {
   return e;
 }
 
+// Launch with programmatic stream serialization: the kernel may start (and
+// stream its static weights) while the previous kernel in the stream drains;
+// it waits for that kernel with griddepcontrol.wait before reading X.
 template <int FMT, int MT, int CH, int RT>
 cudaError_t launch_one(const GemvArgs &a, dim3 grid, int threads, int smem, cudaStream_t st) {
   cudaError_t e = ensure_smem<FMT, MT, CH, RT>(smem);
   if (e != cudaSuccess) return e;
-  gemv_kernel<FMT, MT, CH, RT><<<grid, threads, smem, st>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, MT, CH, RT>, a);
 }
+// Resident CTAs per SM, or -(cudaError_t) when a query failed.
 template <int FMT, int MT, int CH, int RT>
 int occ_one(int threads, int smem) {
   auto k = gemv_kernel<FMT, MT, CH, RT>;
-  if (ensure_smem<FMT, MT, CH, RT>(smem) != cudaSuccess) {
+  cudaError_t e = ensure_smem<FMT, MT, CH, RT>(smem);
+  if (e != cudaSuccess) {
     cudaGetLastError();
-    return 0;
+    return -(int)e;
   }
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, threads, smem) != cudaSuccess) {
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, threads, (size_t)smem);
+  if (e != cudaSuccess) {
     cudaGetLastError();
-    return 0;
+    return -(int)e;
+  }
+  if (nb == 0) {  // record why, for the caller's error message
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, k) == cudaSuccess)
+      snprintf(occ_note(), 160, "regs=%d maxThreadsPerBlock=%d staticSmem=%zu maxDynSmem=%d",
+               fa.numRegs, fa.maxThreadsPerBlock, fa.sharedSizeBytes, fa.maxDynamicSharedSizeBytes);
   }
   return nb;
 }

@@ -78,6 +78,7 @@ def lib() -> C.CDLL:
         "lbc_sm_count": ([], _int),
         "lbc_last_error": ([], C.c_char_p),
         "lbc_device_status": ([_int], _int),
+        "lbc_describe_plan": ([_int, _int, _int, _int, _pp, C.c_char_p, _int], _int),
         "lbc_gemm_w4a16": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_gemm_mxfp4": ([_vp, _int, _int, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_gemm_w4a8_workspace_size": ([_int, _int], C.c_size_t),
@@ -319,6 +320,15 @@ def w4a8_group_acc(a: Int8Acts, w: Int4Weights, isa=None):
                  None if d.zeros is None else d.zeros.data_ptr(), w.n, out.data_ptr(), -1, _stream()),
            "lbc_w4a8_group_acc")
     return out.cpu().numpy() if host else out
+
+
+def describe_plan(kind: str, m: int, n: int, kp: int, params: Params | None = None, isa=None) -> dict:
+    """Kernel configuration the library would launch for this GEMM (for tuning / debugging)."""
+    import json
+    buf = C.create_string_buffer(512)
+    rc = lib().lbc_describe_plan(KIND_IDS[kind], m, n, kp, C.byref(_params(params, isa)), buf, 512)
+    _check(rc, "lbc_describe_plan")
+    return json.loads(buf.value.decode())
 
 
 def device_status(reset: bool = True) -> int:
