@@ -130,42 +130,78 @@ __device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
 }
 
 // ------------------------------------------------------------------ decoders
+// A register holding v that the compiler cannot constant-fold: LOP3 takes one
+// immediate, so "(w & mask) | MAGIC" is a single instruction only when MAGIC
+// lives in a register.
+__device__ __forceinline__ uint32_t opaque(uint32_t v) {
+  uint32_t r;
+  asm volatile("mov.b32 %0, %1;" : "=r"(r) : "r"(v));
+  return r;
+}
+
 // W4A16: one 16-byte chunk (32 codes of one group) against MT tokens.
 // xr[t][j] = (x[lo + j], x[hi + j]) with lo/hi the element bases of the chunk.
+// Two nibbles of w -> the fp32 pair (2^23 + q_a*2^pa, 2^23 + q_b*2^pb) with one
+// lop3 each, written straight into the halves of a 64-bit register pair, then
+// minus (2^23 + z*2^pa, 2^23 + z*2^pb) with one packed add: (q - z) * 2^p.
+template <uint32_t MA, uint32_t MB>
+__device__ __forceinline__ uint64_t nib2(uint32_t w, uint32_t mag, uint64_t negz) {
+  uint64_t r;
+  asm("{\n\t.reg .b32 lo, hi;\n\t.reg .b64 p;\n\t"
+      "lop3.b32 lo, %1, %3, %2, 0xEA;\n\t"
+      "lop3.b32 hi, %1, %4, %2, 0xEA;\n\t"
+      "mov.b64 p, {lo, hi};\n\t"
+      "add.rn.f32x2 %0, p, %5;\n\t}"
+      : "=l"(r)
+      : "r"(w), "r"(mag), "n"(MA), "n"(MB), "l"(negz));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+  return (uint64_t)lo | ((uint64_t)hi << 32);
+}
+
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// W4A16: one 16-byte chunk (32 codes of one group) against MT tokens.
+// xr[t][j] = (x[lo + j], x[hi + j]) as a packed fp32 pair, lo/hi the element
+// bases of the chunk.
 template <int MT>
-__device__ __forceinline__ void dot_w4a16(const uint4 wv, uint32_t z, const float2 (*xr)[16],
-                                          float (&dot)[MT]) {
-  const uint32_t MAG = 0x4B000000u;
-  const float2 nz01 = make_float2(u2f(0xCB000000u | z), u2f(0xCB000000u | (z << 4)));
-  const float2 nz23 = make_float2(u2f(0xCB000000u | (z << 8)), u2f(0xCB000000u | (z << 12)));
-  float2 accA[MT], accB[MT];
+__device__ __forceinline__ void dot_w4a16(const uint4 wv, uint32_t z, const uint64_t (*xr)[16],
+                                          float (&dot)[MT], const uint32_t MAG) {
+  const uint64_t nz01 = pack2(0xCB000000u | z, 0xCB000000u | (z << 4));
+  const uint64_t nz23 = pack2(0xCB000000u | (z << 8), 0xCB000000u | (z << 12));
+  uint64_t accA[MT], accB[MT];
 #pragma unroll
-  for (int t = 0; t < MT; ++t) accA[t] = accB[t] = make_float2(0.f, 0.f);
+  for (int t = 0; t < MT; ++t) accA[t] = accB[t] = 0ull;
   const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const uint32_t w = w4[q];
     const uint32_t h = w >> 16;
-    float2 a = make_float2(u2f((w & 0x000Fu) | MAG), u2f((w & 0x00F0u) | MAG));
-    float2 b = make_float2(u2f((w & 0x0F00u) | MAG), u2f((w & 0xF000u) | MAG));
-    float2 c = make_float2(u2f((h & 0x000Fu) | MAG), u2f((h & 0x00F0u) | MAG));
-    float2 d = make_float2(u2f((h & 0x0F00u) | MAG), u2f((h & 0xF000u) | MAG));
-    a = __fadd2_rn(a, nz01);
-    b = __fadd2_rn(b, nz23);
-    c = __fadd2_rn(c, nz01);
-    d = __fadd2_rn(d, nz23);
+    const uint64_t a = nib2<0x000Fu, 0x00F0u>(w, MAG, nz01);
+    const uint64_t b = nib2<0x0F00u, 0xF000u>(w, MAG, nz23);
+    const uint64_t c = nib2<0x000Fu, 0x00F0u>(h, MAG, nz01);
+    const uint64_t d = nib2<0x0F00u, 0xF000u>(h, MAG, nz23);
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
-      accA[t] = __ffma2_rn(a, xr[t][4 * q + 0], accA[t]);
-      accB[t] = __ffma2_rn(b, xr[t][4 * q + 1], accB[t]);
-      accA[t] = __ffma2_rn(c, xr[t][4 * q + 2], accA[t]);
-      accB[t] = __ffma2_rn(d, xr[t][4 * q + 3], accB[t]);
+      accA[t] = ffma2(a, xr[t][4 * q + 0], accA[t]);
+      accB[t] = ffma2(b, xr[t][4 * q + 1], accB[t]);
+      accA[t] = ffma2(c, xr[t][4 * q + 2], accA[t]);
+      accB[t] = ffma2(d, xr[t][4 * q + 3], accB[t]);
     }
   }
 #pragma unroll
   for (int t = 0; t < MT; ++t)
-    dot[t] = fmaf(accB[t].y, 1.0f / 4096.0f,
-                  fmaf(accB[t].x, 1.0f / 256.0f, fmaf(accA[t].y, 1.0f / 16.0f, accA[t].x)));
+    dot[t] = fmaf(hi_f(accB[t]), 1.0f / 4096.0f,
+                  fmaf(lo_f(accB[t]), 1.0f / 256.0f, fmaf(hi_f(accA[t]), 1.0f / 16.0f, lo_f(accA[t]))));
 }
 
 // MXFP4: one 16-byte chunk = one block of 32 E2M1 codes. The result is
@@ -173,14 +209,14 @@ __device__ __forceinline__ void dot_w4a16(const uint4 wv, uint32_t z, const floa
 // Codes are mapped through two 8-entry byte tables (prmt) to 16 + 2*e2m1(q),
 // a value in [4, 28], then to fp32 with the 2^23 magic number.
 template <int MT>
-__device__ __forceinline__ void dot_mxfp4(const uint4 wv, const float2 (*xr)[16], float (&dot)[MT]) {
+__device__ __forceinline__ void dot_mxfp4(const uint4 wv, const uint64_t (*xr)[16], float (&dot)[MT],
+                                          const uint32_t MAGIC) {
   const uint32_t TP0 = 0x13121110u, TP1 = 0x1C181614u;  // 16 + {0,1,2,3}, 16 + {4,6,8,12}
   const uint32_t TN0 = 0x0D0E0F10u, TN1 = 0x04080A0Cu;  // 16 - {0,1,2,3}, 16 - {4,6,8,12}
-  const uint32_t MAGIC = 0x4B000000u;
-  const float2 NB = make_float2(-8388624.0f, -8388624.0f);  // -(2^23 + 16)
-  float2 accA[MT], accB[MT];
+  const uint64_t NB = pack2(0xCB000010u, 0xCB000010u);   // -(2^23 + 16) twice
+  uint64_t accA[MT], accB[MT];
 #pragma unroll
-  for (int t = 0; t < MT; ++t) accA[t] = accB[t] = make_float2(0.f, 0.f);
+  for (int t = 0; t < MT; ++t) accA[t] = accB[t] = 0ull;
   const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -194,19 +230,27 @@ __device__ __forceinline__ void dot_mxfp4(const uint4 wv, const float2 (*xr)[16]
       const uint32_t neg = prmt(TN0, TN1, sel);
       const uint32_t msk = prmt(w4s, w, half ? 0xFBEAu : 0xD9C8u);  // 0xFF where the code is negative
       const uint32_t val = (pos & ~msk) | (neg & msk);               // bytes: 16 + 2*e2m1
-      float2 p0 = make_float2(u2f(prmt(val, MAGIC, 0x7540u)), u2f(prmt(val, MAGIC, 0x7541u)));
-      float2 p1 = make_float2(u2f(prmt(val, MAGIC, 0x7542u)), u2f(prmt(val, MAGIC, 0x7543u)));
-      p0 = __fadd2_rn(p0, NB);
-      p1 = __fadd2_rn(p1, NB);
+      uint64_t p0, p1;
+      asm("{\n\t.reg .b32 a, b, c, d;\n\t.reg .b64 u, v;\n\t"
+          "prmt.b32 a, %2, %3, 0x7540;\n\t"
+          "prmt.b32 b, %2, %3, 0x7541;\n\t"
+          "prmt.b32 c, %2, %3, 0x7542;\n\t"
+          "prmt.b32 d, %2, %3, 0x7543;\n\t"
+          "mov.b64 u, {a, b};\n\t"
+          "mov.b64 v, {c, d};\n\t"
+          "add.rn.f32x2 %0, u, %4;\n\t"
+          "add.rn.f32x2 %1, v, %4;\n\t}"
+          : "=l"(p0), "=l"(p1)
+          : "r"(val), "r"(MAGIC), "l"(NB));
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        accA[t] = __ffma2_rn(p0, xr[t][4 * q + 2 * half + 0], accA[t]);
-        accB[t] = __ffma2_rn(p1, xr[t][4 * q + 2 * half + 1], accB[t]);
+        accA[t] = ffma2(p0, xr[t][4 * q + 2 * half + 0], accA[t]);
+        accB[t] = ffma2(p1, xr[t][4 * q + 2 * half + 1], accB[t]);
       }
     }
   }
 #pragma unroll
-  for (int t = 0; t < MT; ++t) dot[t] = (accA[t].x + accA[t].y) + (accB[t].x + accB[t].y);
+  for (int t = 0; t < MT; ++t) dot[t] = (lo_f(accA[t]) + hi_f(accA[t])) + (lo_f(accB[t]) + hi_f(accB[t]));
 }
 
 // 2^(e-128) as fp32: half the E8M0 block scale (the MXFP4 decoder returns 2x).
@@ -306,7 +350,7 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
   // activations (written by the previous kernel, if any) of this thread's
   // chunks, resident in registers for the whole kernel
   pdl_wait_prior_grid();
-  float2 xr[CH][MT][16];
+  uint64_t xr[CH][MT][16];
   uint32_t xl[CH][MT][4], xh[CH][MT][4];
   int xsum[CH][MT];
   (void)xr; (void)xl; (void)xh; (void)xsum;
@@ -347,23 +391,37 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
             l4 = __ldg(pl + q);
             h4 = __ldg(ph + q);
           }
-          xr[i][t][4 * q + 0] = make_float2(l4.x, h4.x);
-          xr[i][t][4 * q + 1] = make_float2(l4.y, h4.y);
-          xr[i][t][4 * q + 2] = make_float2(l4.z, h4.z);
-          xr[i][t][4 * q + 3] = make_float2(l4.w, h4.w);
+          xr[i][t][4 * q + 0] = pack2(__float_as_uint(l4.x), __float_as_uint(h4.x));
+          xr[i][t][4 * q + 1] = pack2(__float_as_uint(l4.y), __float_as_uint(h4.y));
+          xr[i][t][4 * q + 2] = pack2(__float_as_uint(l4.z), __float_as_uint(h4.z));
+          xr[i][t][4 * q + 3] = pack2(__float_as_uint(l4.w), __float_as_uint(h4.w));
         }
       }
     }
   }
 
+  // Per-thread chunk bookkeeping, fixed for the kernel. A chunk past the end
+  // of the segment (c >= Cs) is clamped onto the last real chunk: its
+  // activations are zero, so it adds exactly 0 and the inner loop needs no
+  // bounds checks.
+  int ch_off[CH], ch_g[CH], ch_kc[CH];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = min(tin + i * a.tpr, Cs - 1);
+    ch_off[i] = c << 4;
+    ch_kc[i] = (k0 >> 5) + c;
+    ch_g[i] = ch_kc[i] >> 2;
+  }
+  const uint32_t MAG = opaque(0x4B000000u);
+
   bool ok = true;
+  int s = 0;
+  uint32_t ph = 0;
   for (int it = 0; it < my_tiles; ++it) {
-    const int s = it % S;
-    const uint32_t ph = (uint32_t)(it / S) & 1u;
     // refill the stage released by tile it-1 with tile it-1+S
     if (tid == 0 && it >= 1 && it - 1 + S < my_tiles) {
-      const int sp = (it - 1) % S;
-      const uint32_t php = (uint32_t)((it - 1) / S) & 1u;
+      const int sp = (s == 0) ? S - 1 : s - 1;
+      const uint32_t php = (s == 0) ? (ph ^ 1u) : ph;
       if (ok) ok = !(*abort_flag) && mbar_wait(&empty[sp], php, a.status);
       if (ok)
         issue(it - 1 + S);
@@ -376,44 +434,44 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
     const uint8_t *st = stage_base + s * L.stage_bytes;
 
     // per-(row, chunk) scale and zero point: from the stage when TMA brought
-    // them, else fetched from global memory before waiting on the tile
+    // them, else from global memory (fetched before waiting on the tile).
+    // Rows past the end of a tail tile read clamped / stale values; their
+    // results are never written.
     float sc[RT][CH];
     uint32_t zz[RT][CH];
-    auto fetch_meta = [&](bool from_smem) {
+    if (!tm) {
 #pragma unroll
       for (int j = 0; j < RT; ++j) {
-        const int r = team + j * RP;
-        const int n = r0 + r;
-        const bool rv = r < rows;
+        const int n = min(r0 + team + j * RP, a.N - 1);
 #pragma unroll
         for (int i = 0; i < CH; ++i) {
-          const int c = tin + i * a.tpr;
-          const int kc = (k0 >> 5) + c;
-          sc[j][i] = 0.f;
-          zz[j][i] = 8u;
-          if (rv && c < Cs) {
-            if (FMT == FMT_MXFP4) {
-              const uint32_t e = from_smem ? st[MM.sc_off + r * NB32 + kc] : __ldg(a.e8m0 + (size_t)n * NB32 + kc);
-              sc[j][i] = e8m0_half_scale(e);
-            } else {
-              const int g = kc >> 2;
-              if (from_smem) {
-                sc[j][i] = reinterpret_cast<const float *>(st + MM.sc_off)[r * G + g];
-                if (has_z) zz[j][i] = st[MM.z_off + r * G + g];
-              } else {
-                sc[j][i] = __ldg(a.scales + (size_t)n * G + g);
-                if (has_z) zz[j][i] = __ldg(a.zeros + (size_t)n * G + g);
-              }
-            }
+          if (FMT == FMT_MXFP4) {
+            sc[j][i] = e8m0_half_scale(__ldg(a.e8m0 + (size_t)n * NB32 + ch_kc[i]));
+          } else {
+            sc[j][i] = __ldg(a.scales + (size_t)n * G + ch_g[i]);
+            zz[j][i] = has_z ? (uint32_t)__ldg(a.zeros + (size_t)n * G + ch_g[i]) : 8u;
           }
         }
       }
-    };
-    if (!tm) fetch_meta(false);
+    }
 
     if (ok) ok = !(*abort_flag) && mbar_wait(&full[s], ph, a.status);
     if (!ok) *abort_flag = 1;
-    if (tm) fetch_meta(true);
+    if (tm) {
+#pragma unroll
+      for (int j = 0; j < RT; ++j) {
+        const int r = team + j * RP;
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          if (FMT == FMT_MXFP4) {
+            sc[j][i] = e8m0_half_scale(st[MM.sc_off + r * NB32 + ch_kc[i]]);
+          } else {
+            sc[j][i] = reinterpret_cast<const float *>(st + MM.sc_off)[r * G + ch_g[i]];
+            zz[j][i] = has_z ? (uint32_t)st[MM.z_off + r * G + ch_g[i]] : 8u;
+          }
+        }
+      }
+    }
 
     float part[RT][MT];
 #pragma unroll
@@ -421,47 +479,40 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
 #pragma unroll
       for (int t = 0; t < MT; ++t) part[j][t] = 0.f;
 
-    if (ok) {
 #pragma unroll
-      for (int j = 0; j < RT; ++j) {
-        const int r = team + j * RP;
-        if (r < rows) {
+    for (int j = 0; j < RT; ++j) {
+      const uint8_t *rowp = st + (team + j * RP) * SB;
 #pragma unroll
-          for (int i = 0; i < CH; ++i) {
-            const int c = tin + i * a.tpr;
-            if (c < Cs) {
-              const uint4 wv = lds128(st + r * SB + (c << 4));
-              if (FMT == FMT_W4A8) {
-                int acc[MT];
+      for (int i = 0; i < CH; ++i) {
+        const uint4 wv = lds128(rowp + ch_off[i]);
+        if (FMT == FMT_W4A8) {
+          int acc[MT];
 #pragma unroll
-                for (int t = 0; t < MT; ++t) acc[t] = 0;
-                const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+          for (int t = 0; t < MT; ++t) acc[t] = 0;
+          const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const uint32_t lo = w4[q] & 0x0F0F0F0Fu;
-                  const uint32_t hi = (w4[q] >> 4) & 0x0F0F0F0Fu;
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t lo = w4[q] & 0x0F0F0F0Fu;
+            const uint32_t hi = (w4[q] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-                  for (int t = 0; t < MT; ++t) {
-                    acc[t] = dp4a_us(lo, xl[i][t][q], acc[t]);
-                    acc[t] = dp4a_us(hi, xh[i][t][q], acc[t]);
-                  }
-                }
-#pragma unroll
-                for (int t = 0; t < MT; ++t) {
-                  const int d = acc[t] - (int)zz[j][i] * xsum[i][t];
-                  part[j][t] = fmaf((float)d, sc[j][i], part[j][t]);
-                }
-              } else {
-                float dot[MT];
-                if (FMT == FMT_W4A16)
-                  dot_w4a16<MT>(wv, zz[j][i], xr[i], dot);
-                else
-                  dot_mxfp4<MT>(wv, xr[i], dot);
-#pragma unroll
-                for (int t = 0; t < MT; ++t) part[j][t] = fmaf(dot[t], sc[j][i], part[j][t]);
-              }
+            for (int t = 0; t < MT; ++t) {
+              acc[t] = dp4a_us(lo, xl[i][t][q], acc[t]);
+              acc[t] = dp4a_us(hi, xh[i][t][q], acc[t]);
             }
           }
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            const int d = acc[t] - (int)zz[j][i] * xsum[i][t];
+            part[j][t] = fmaf((float)d, sc[j][i], part[j][t]);
+          }
+        } else {
+          float dot[MT];
+          if (FMT == FMT_W4A16)
+            dot_w4a16<MT>(wv, zz[j][i], xr[i], dot, MAG);
+          else
+            dot_mxfp4<MT>(wv, xr[i], dot, MAG);
+#pragma unroll
+          for (int t = 0; t < MT; ++t) part[j][t] = fmaf(dot[t], sc[j][i], part[j][t]);
         }
       }
     }
@@ -509,6 +560,10 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
         else
           *dst = val;
       }
+    }
+    if (++s == S) {
+      s = 0;
+      ph ^= 1u;
     }
   }
 }
