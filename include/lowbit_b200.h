@@ -121,6 +121,23 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw,
                   const float *scales, const uint8_t *zeros, int N, float *y,
                   const lbc_params *p, void *workspace, void *stream);
 
+/* W4A8 with fp32 X for callers that cannot allocate device memory: no
+ * counterpart in the reference. Identical results to lbc_gemm_w4a8, but the
+ * activation scratch lives in a fixed LBC_NOALLOC_SCRATCH_BYTES array inside
+ * this library (one per GPU, held until exit) instead of a caller workspace or
+ * an allocation, so nothing is allocated on this path. It serves components
+ * that receive only input/output pointers and have no allocator or workspace
+ * to draw from, and latency-bound loops that must not enter the allocator.
+ * Problems needing more than the array (lbc_gemm_w4a8_workspace_size(M, Kp) >
+ * LBC_NOALLOC_SCRATCH_BYTES) return LBC_ERR_SHAPE without launching. The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress) with
+ * that device current; make it before any stream capture. All calls on a
+ * device share the array: calls whose GPU work may overlap race on it. */
+#define LBC_NOALLOC_SCRATCH_BYTES (4 << 20)
+int lbc_gemm_w4a8_noalloc(const float *x, int M, int Kp, const uint8_t *qw,
+                          const float *scales, const uint8_t *zeros, int N, float *y,
+                          const lbc_params *p, void *stream);
+
 /* W4A8 on pre-quantized activations: replaces lb_gemm_w4a8_q
  * (src/lowbit/csrc/lowbit.h:113-116, dispatch.c:259-268). */
 int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum,

@@ -263,6 +263,8 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum) {
 
 }  // namespace
 
+void lbc::set_last_error(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
+
 // ====================================================================== C ABI
 extern "C" {
 
