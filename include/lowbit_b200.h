@@ -96,6 +96,13 @@ int lbc_device_status(int reset);
 int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char *buf,
                       int buflen);
 
+/* Device self-test of the tensor-core building blocks (TMEM allocation, MMA
+ * with A in tensor memory and B in shared memory, accumulator readback):
+ * writes D[128,16] = A.B^T for fixed small-integer A, B into out (int32,
+ * 2048 entries, device memory); kind 0 = bf16 x bf16 -> f32 (K=32),
+ * 1 = s8 x s8 -> s32 (K=64). Diagnostic; no reference counterpart. */
+int lbc_tc_selftest(int kind, int32_t *out, void *stream);
+
 /* ---- GEMMs ---- */
 
 /* W4A16: replaces lb_gemm_w4a16 (src/lowbit/csrc/lowbit.h:104-106,

@@ -286,6 +286,14 @@ int lbc_device_status(int reset) {
   return v;
 }
 
+int lbc_tc_selftest(int kind, int32_t *out, void *stream) {
+  if ((kind != 0 && kind != 1) || !out) return fail(LBC_ERR_SHAPE, "kind must be 0 or 1, out non-NULL");
+  if (int rc = device_gate()) return rc;
+  cudaError_t e = lbc::launch_tc_selftest(kind, out, dev_info().status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda("tc_selftest launch", e);
+  return 0;
+}
+
 int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char *buf, int buflen) {
   if (kind < 0 || kind > 2) return fail(LBC_ERR_SHAPE, "kind must be 0 (w4a16), 1 (mxfp4) or 2 (w4a8)");
   if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;

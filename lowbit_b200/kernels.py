@@ -79,6 +79,7 @@ def lib() -> C.CDLL:
         "lbc_last_error": ([], C.c_char_p),
         "lbc_device_status": ([_int], _int),
         "lbc_describe_plan": ([_int, _int, _int, _int, _pp, C.c_char_p, _int], _int),
+        "lbc_tc_selftest": ([_int, _vp, _vp], _int),
         "lbc_gemm_w4a16": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_gemm_mxfp4": ([_vp, _int, _int, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_gemm_w4a8_workspace_size": ([_int, _int], C.c_size_t),
@@ -329,6 +330,14 @@ def describe_plan(kind: str, m: int, n: int, kp: int, params: Params | None = No
     rc = lib().lbc_describe_plan(KIND_IDS[kind], m, n, kp, C.byref(_params(params, isa)), buf, 512)
     _check(rc, "lbc_describe_plan")
     return json.loads(buf.value.decode())
+
+
+def tc_selftest(kind: int):
+    """D[128,16] from the tensor-core self-test kernel (kind 0 bf16, 1 int8) as int32 numpy."""
+    torch = _torch()
+    out = torch.full((128, 16), -12345, dtype=torch.int32, device="cuda")
+    _check(lib().lbc_tc_selftest(kind, out.data_ptr(), _stream()), "lbc_tc_selftest")
+    return out.cpu().numpy()
 
 
 def device_status(reset: bool = True) -> int:
