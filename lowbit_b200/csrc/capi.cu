@@ -252,13 +252,28 @@ int device_gate() {
   return 0;
 }
 
-size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum) {
+size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *off_tc = nullptr) {
   const size_t xq_bytes = ((size_t)M * Kp + 255) / 256 * 256;
   const size_t xs_bytes = ((size_t)M * 4 + 255) / 256 * 256;
   const size_t as_bytes = ((size_t)M * (Kp / 128) * 4 + 255) / 256 * 256;
+  const size_t tc_bytes = (lbc::tc_bglob_bytes(lbc::FMT_W4A8, M, Kp) + 255) / 256 * 256;
   if (off_xs) *off_xs = xq_bytes;
   if (off_asum) *off_asum = xq_bytes + xs_bytes;
-  return xq_bytes + xs_bytes + as_bytes;
+  if (off_tc) *off_tc = xq_bytes + xs_bytes + as_bytes;
+  return xq_bytes + xs_bytes + as_bytes + tc_bytes;
+}
+
+bool want_tc(const lbc_params *p) { return p && p->isa == LBC_PATH_TCGEN05; }
+
+int run_tc(lbc::TcCall c, cudaStream_t st) {
+  const DevInfo di = dev_info();
+  c.status = di.status;
+  c.sms = di.sms;
+  c.smem_optin = di.smem_optin;
+  char msg[256] = "";
+  const int rc = lbc::tc_gemm(c, st, msg, sizeof msg);
+  if (rc < 0) return fail(rc, msg);
+  return rc;
 }
 
 }  // namespace
@@ -318,6 +333,12 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_tc(p)) {
+    lbc::TcCall c{};
+    c.fmt = lbc::FMT_W4A16; c.x = x; c.qw = qw; c.scales = scales; c.zeros = zeros; c.y = y;
+    c.M = M; c.N = N; c.Kp = Kp;
+    return run_tc(c, static_cast<cudaStream_t>(stream));
+  }
   lbc::GemvArgs a{};
   a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
   a.M = M; a.N = N; a.Kp = Kp;
@@ -330,6 +351,12 @@ int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8
   if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_tc(p)) {
+    lbc::TcCall c{};
+    c.fmt = lbc::FMT_MXFP4; c.x = x; c.qw = qw; c.e8m0 = e8m0; c.y = y;
+    c.M = M; c.N = N; c.Kp = Kp;
+    return run_tc(c, static_cast<cudaStream_t>(stream));
+  }
   lbc::GemvArgs a{};
   a.x = x; a.qw = qw; a.e8m0 = e8m0; a.y = y;
   a.M = M; a.N = N; a.Kp = Kp;
@@ -354,6 +381,12 @@ int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int 
   if (!xq || !xs || !asum || !qw || !scales || !y || !al16(xq) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_tc(p)) {
+    lbc::TcCall c{};
+    c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
+    c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
+    return run_tc(c, static_cast<cudaStream_t>(stream));
+  }
   lbc::GemvArgs a{};
   a.xq = xq; a.xs = xs; a.asum = asum; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
   a.M = M; a.N = N; a.Kp = Kp;
@@ -375,8 +408,8 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
     return fail(LBC_ERR_SHAPE, "workspace must be 256-byte aligned");
   if (int rc = device_gate()) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  size_t off_xs, off_as;
-  const size_t bytes = w4a8_ws_layout(M, Kp, &off_xs, &off_as);
+  size_t off_xs, off_as, off_tc;
+  const size_t bytes = w4a8_ws_layout(M, Kp, &off_xs, &off_as, &off_tc);
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   bool owned = false;
   if (!ws) {
@@ -394,7 +427,14 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
   int rc = 0;
   cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, st);
   if (e != cudaSuccess) rc = fail_cuda("quant_act_int8 launch", e);
-  if (rc == 0) {
+  if (rc == 0 && want_tc(p)) {
+    lbc::TcCall c{};
+    c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
+    c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
+    c.bscratch = ws + off_tc;
+    c.bscratch_bytes = bytes - off_tc;
+    rc = run_tc(c, st);
+  } else if (rc == 0) {
     lbc::GemvArgs a{};
     a.xq = xq; a.xs = xs; a.asum = asum; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
     a.M = M; a.N = N; a.Kp = Kp;

@@ -15,6 +15,28 @@ cudaError_t launch_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, 
 
 cudaError_t launch_tc_selftest(int kind, int32_t *out, int *status, cudaStream_t st);
 
+// one tensor-core GEMM call (tcgemm.cu)
+struct TcCall {
+  int fmt;                 // FMT_W4A16 / FMT_MXFP4 / FMT_W4A8 (gemv.cuh ids: 0 / 1 / 2)
+  const float *x;          // fp formats: [M, Kp]
+  const int8_t *xq;        // W4A8: [M, Kp]
+  const float *xs;         // W4A8: [M]
+  const int32_t *asum;     // W4A8: [M, Kp/128]
+  const uint8_t *qw;
+  const float *scales;
+  const uint8_t *zeros;
+  const uint8_t *e8m0;
+  float *y;
+  int M, N, Kp;
+  void *bscratch;          // activation blocks (tc_bglob_bytes), or nullptr
+  size_t bscratch_bytes;
+  int *status;
+  int sms, smem_optin;
+};
+size_t tc_bglob_bytes(int fmt, int M, int Kp);
+// returns LBC_PATH_TCGEN05 or a negative LBC_ERR_* with a message in err
+int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen);
+
 // records `msg` as the text lbc_last_error() returns on this thread
 void set_last_error(const char *msg);
 
