@@ -256,7 +256,7 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *o
   const size_t xq_bytes = ((size_t)M * Kp + 255) / 256 * 256;
   const size_t xs_bytes = ((size_t)M * 4 + 255) / 256 * 256;
   const size_t as_bytes = ((size_t)M * (Kp / 128) * 4 + 255) / 256 * 256;
-  const size_t tc_bytes = (lbc::tc_bglob_bytes(lbc::FMT_W4A8, M, Kp) + 255) / 256 * 256;
+  const size_t tc_bytes = (lbc::tc_scratch_bytes(lbc::FMT_W4A8, M, Kp, std::max(1, dev_info().sms)) + 255) / 256 * 256;
   if (off_xs) *off_xs = xq_bytes;
   if (off_asum) *off_asum = xq_bytes + xs_bytes;
   if (off_tc) *off_tc = xq_bytes + xs_bytes + as_bytes;
@@ -431,8 +431,8 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
-    c.bscratch = ws + off_tc;
-    c.bscratch_bytes = bytes - off_tc;
+    c.scratch = ws + off_tc;
+    c.scratch_bytes = bytes - off_tc;
     rc = run_tc(c, st);
   } else if (rc == 0) {
     lbc::GemvArgs a{};

@@ -28,12 +28,14 @@ struct TcCall {
   const uint8_t *e8m0;
   float *y;
   int M, N, Kp;
-  void *bscratch;          // activation blocks (tc_bglob_bytes), or nullptr
-  size_t bscratch_bytes;
+  void *scratch;           // fixup scratch (tc_scratch_bytes), or nullptr
+  size_t scratch_bytes;
   int *status;
   int sms, smem_optin;
 };
-size_t tc_bglob_bytes(int fmt, int M, int Kp);
+// scratch for format `fmt` (FMT_* id), M tokens, Kp columns when the grid
+// has `ctas` CTAs (at most the SM count)
+size_t tc_scratch_bytes(int fmt, int M, int Kp, int ctas);
 // returns LBC_PATH_TCGEN05 or a negative LBC_ERR_* with a message in err
 int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen);
 

@@ -1,4 +1,6 @@
 // Tensor-core GEMM: instantiations, planning and launch (see tcgemm.cuh).
+#include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <map>
 #include <mutex>
@@ -15,21 +17,39 @@ int tc_mt(int M) { return M <= 4 ? 4 : (M <= 8 ? 8 : 16); }
 int tc_npiece(int fmt) { return fmt == FMT_W4A8 ? 1 : 3; }
 int tc_bblock(int fmt, int mt) { return tc_nmma(mt, tc_npiece(fmt)) * 256 * (fmt == FMT_W4A8 ? 1 : 2); }
 
-template <int FMT, int NP>
-cudaError_t dispatch_mt(int mt, const CUtensorMap &map, const TcArgs &a, int chunks, int grid_x, int smem,
-                        cudaStream_t st) {
-  switch (mt) {
-    case 4: return tc_launch_one<FMT, 4, NP>(map, a, chunks, grid_x, smem, st);
-    case 8: return tc_launch_one<FMT, 8, NP>(map, a, chunks, grid_x, smem, st);
-    default: return tc_launch_one<FMT, 16, NP>(map, a, chunks, grid_x, smem, st);
-  }
+// B blocks come from a preparation kernel (TMA-fed) for 8 or more tokens per
+// chunk; with 4 the row warps build them in shared memory.
+bool tc_btma(int mt) { return mt > 4; }
+
+size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+
+// scratch: partial rows [chunks][ctas][128][mt] floats, flags [chunks][ctas],
+// then (TMA-fed B) activation blocks [chunks][nkb][bblock]
+size_t scratch_bytes(int fmt, int M, int Kp, int ctas) {
+  const int mt = tc_mt(M);
+  const size_t chunks = (size_t)((M + mt - 1) / mt);
+  const size_t part = round256(chunks * ctas * TC_ROWS * mt * sizeof(float));
+  const size_t flags = round256(chunks * ctas * sizeof(uint32_t));
+  const size_t nkb = (size_t)((Kp + TC_KB - 1) / TC_KB);
+  const size_t bglob = tc_btma(mt) ? round256(chunks * nkb * tc_bblock(fmt, mt)) : 0;
+  return part + flags + bglob;
 }
 
-// Activation-block scratch for calls without a workspace: one grow-only buffer
-// per (device, stream), so back-to-back GEMMs on a stream issue no allocation
-// between them (an allocation would break their programmatic overlap). The
-// buffers live until the process exits. During stream capture a growth falls
-// back to a stream-ordered allocation for that call.
+// A value no earlier call in this process used: partial-tile flags carry it.
+uint32_t next_epoch() {
+  static std::atomic<uint32_t> ctr{(uint32_t)(std::chrono::steady_clock::now().time_since_epoch().count() &
+                                              0x3FFFFFFF) | 1u};
+  uint32_t e;
+  do {
+    e = ctr.fetch_add(1);
+  } while (e == 0u);
+  return e;
+}
+
+// Fixup scratch for calls without a workspace: one grow-only, zero-initialised
+// buffer per (device, stream), so back-to-back GEMMs on a stream issue no
+// allocation between them. The buffers live until the process exits. During
+// stream capture a growth falls back to a stream-ordered allocation.
 void *cached_scratch(size_t need, cudaStream_t st, bool *owned) {
   static std::mutex mu;
   static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
@@ -60,27 +80,33 @@ void *cached_scratch(size_t need, cudaStream_t st, bool *owned) {
     cudaGetLastError();
     return nullptr;
   }
+  cudaMemsetAsync(p, 0, need, st);
   slot = {p, need};
   return p;
 }
 
+template <int FMT, int NP>
+cudaError_t dispatch_mt(int mt, const CUtensorMap &map, const TcArgs &a, int chunks, int grid_x, int smem,
+                        cudaStream_t st) {
+  switch (mt) {
+    case 4: return tc_launch_one<FMT, 4, NP, false>(map, a, chunks, grid_x, smem, st);
+    case 8: return tc_launch_one<FMT, 8, NP, true>(map, a, chunks, grid_x, smem, st);
+    default: return tc_launch_one<FMT, 16, NP, true>(map, a, chunks, grid_x, smem, st);
+  }
+}
+
 }  // namespace
 
-size_t tc_bglob_bytes(int fmt, int M, int Kp) {
-  const int mt = tc_mt(M);
-  const size_t chunks = (size_t)((M + mt - 1) / mt);
-  const size_t nkb = (size_t)((Kp + 255) / 256);
-  return chunks * nkb * (size_t)tc_bblock(fmt, mt);
-}
+size_t tc_scratch_bytes(int fmt, int M, int Kp, int ctas) { return scratch_bytes(fmt, M, Kp, ctas); }
 
 int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   const int fmt = c.fmt;
   const int mt = tc_mt(c.M);
-  const int np = tc_npiece(fmt);
-  const int nmma = tc_nmma(mt, np);
   const int chunks = (c.M + mt - 1) / mt;
   const int bbytes = tc_bblock(fmt, mt);
   TcArgs a{};
+  a.x = c.x;
+  a.xq = c.xq;
   a.scales = c.scales;
   a.zeros = c.zeros;
   a.e8m0 = c.e8m0;
@@ -95,55 +121,45 @@ int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   a.ntiles = (c.N + TC_ROWS - 1) / TC_ROWS;
   a.units = a.nkb * a.ntiles;
   a.b_block_bytes = bbytes;
-  a.mt = mt;
   a.status = c.status;
-  const int per_stage = TC_WBYTES + (bbytes + 127) / 128 * 128;
+  a.epoch = next_epoch();
   int stages = 6;
-  while (stages > 2 && tc_smem_layout(stages, bbytes).total > c.smem_optin) --stages;
+  while (stages > 2 && tc_smem_layout(stages, bbytes, mt).total > c.smem_optin) --stages;
   a.stages = stages;
-  const int smem = tc_smem_layout(stages, bbytes).total;
-  (void)per_stage;
+  const int smem = tc_smem_layout(stages, bbytes, mt).total;
   if (smem > c.smem_optin) {
     snprintf(err, errlen, "tensor-core tile does not fit in shared memory");
     return LBC_ERR_PARAMS;
   }
+  const int grid_x = a.units < c.sms ? a.units : c.sms;
   CUtensorMap map;
   cudaError_t e = make_weight_map(&map, c.qw, c.N, c.Kp);
   if (e != cudaSuccess) {
     snprintf(err, errlen, "cuTensorMapEncodeTiled failed for the weight tensor");
     return LBC_ERR_CUDA;
   }
-  const size_t need = tc_bglob_bytes(fmt, c.M, c.Kp);
-  uint8_t *bglob = static_cast<uint8_t *>(c.bscratch);
+  const size_t need = scratch_bytes(fmt, c.M, c.Kp, grid_x);
+  uint8_t *scr = static_cast<uint8_t *>(c.scratch);
   bool owned = false;
-  if (!bglob || c.bscratch_bytes < need) {
-    bglob = static_cast<uint8_t *>(cached_scratch(need, st, &owned));
-    if (!bglob) {
-      snprintf(err, errlen, "allocation of %zu bytes of activation blocks failed", need);
+  if (!scr || c.scratch_bytes < need) {
+    scr = static_cast<uint8_t *>(cached_scratch(need, st, &owned));
+    if (!scr) {
+      snprintf(err, errlen, "allocation of %zu bytes of GEMM scratch failed", need);
       return LBC_ERR_ALLOC;
     }
   }
-  a.bglob = bglob;
-  const dim3 pgrid(a.nkb, chunks, 1);
+  const size_t part_bytes = round256((size_t)chunks * grid_x * TC_ROWS * mt * sizeof(float));
+  const size_t flag_bytes = round256((size_t)chunks * grid_x * sizeof(uint32_t));
+  a.partial = reinterpret_cast<float *>(scr);
+  a.flags = reinterpret_cast<uint32_t *>(scr + part_bytes);
+  a.bglob = tc_btma(mt) ? scr + part_bytes + flag_bytes : nullptr;
   if (fmt == FMT_W4A16)
-    e = launch_pdl(tc_prep_kernel<FMT_W4A16>, pgrid, dim3(256), 0, st, c.x, (const int8_t *)nullptr, c.M, c.Kp,
-                   a.nkb, mt, nmma, np, bglob, bbytes, c.y, c.N);
+    e = dispatch_mt<FMT_W4A16, 3>(mt, map, a, chunks, grid_x, smem, st);
   else if (fmt == FMT_MXFP4)
-    e = launch_pdl(tc_prep_kernel<FMT_MXFP4>, pgrid, dim3(256), 0, st, c.x, (const int8_t *)nullptr, c.M, c.Kp,
-                   a.nkb, mt, nmma, np, bglob, bbytes, c.y, c.N);
+    e = dispatch_mt<FMT_MXFP4, 3>(mt, map, a, chunks, grid_x, smem, st);
   else
-    e = launch_pdl(tc_prep_kernel<FMT_W4A8>, pgrid, dim3(256), 0, st, (const float *)nullptr, c.xq, c.M, c.Kp,
-                   a.nkb, mt, nmma, np, bglob, bbytes, c.y, c.N);
-  if (e == cudaSuccess) {
-    const int grid_x = a.units < c.sms ? a.units : c.sms;
-    if (fmt == FMT_W4A16)
-      e = dispatch_mt<FMT_W4A16, 3>(mt, map, a, chunks, grid_x, smem, st);
-    else if (fmt == FMT_MXFP4)
-      e = dispatch_mt<FMT_MXFP4, 3>(mt, map, a, chunks, grid_x, smem, st);
-    else
-      e = dispatch_mt<FMT_W4A8, 1>(mt, map, a, chunks, grid_x, smem, st);
-  }
-  if (owned) cudaFreeAsync(bglob, st);
+    e = dispatch_mt<FMT_W4A8, 1>(mt, map, a, chunks, grid_x, smem, st);
+  if (owned) cudaFreeAsync(scr, st);
   if (e != cudaSuccess) {
     snprintf(err, errlen, "tensor-core GEMM launch: %s", cudaGetErrorString(e));
     return LBC_ERR_CUDA;
