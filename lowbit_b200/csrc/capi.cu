@@ -216,7 +216,69 @@ bool meta_aligned(int fmt, const lbc::GemvArgs &a) {
   return al16(a.scales) && (a.zeros == nullptr || al16(a.zeros));
 }
 
+// ------------------------------------------------------------------ decode plan
+// The register-streamed kernel (gemv_rows.cuh) serves one or two tokens of
+// the int4 formats when no staged-kernel tiling was requested (mr, nr, kb,
+// order unset; nb = CTAs per SM is honoured).
+struct RowsPlan {
+  int mt = 1, ch = 1, r = 4, threads = 128, grid = 1, cps = 4;
+};
+
+bool rows_eligible(int fmt, int M, int Kp, const lbc_params *p) {
+  // MXFP4's table decode is ALU-heavier; its staged kernel is faster at M = 1
+  if (M > 2 || fmt == lbc::FMT_MXFP4) return false;
+  if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0)) return false;
+  const int Cs = Kp / 32;
+  return Cs <= lbc::ROWS_MAX_WARPS * 32 * (M == 1 ? 4 : 2);
+}
+
+int rows_occupancy_cached(int fmt, int mt, int ch, int r, int threads) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  int d = 0;
+  cudaGetDevice(&d);
+  const uint64_t key = ((uint64_t)(d & 63) << 40) | ((uint64_t)(fmt & 3) << 32) | ((uint64_t)(mt & 15) << 24) |
+                       ((uint64_t)(ch & 15) << 16) | ((uint64_t)(r & 255) << 8) | (uint64_t)(threads >> 5);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int v = lbc::rows_occupancy(fmt, mt, ch, r, threads);
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = v;
+  return v;
+}
+
+int plan_rows(int fmt, int M, int N, int Kp, const lbc_params *p, RowsPlan &P) {
+  const DevInfo di = dev_info();
+  const int Cs = Kp / 32;
+  const int nw = std::min(lbc::ROWS_MAX_WARPS, ceil_div(Cs, 32));
+  int ch = ceil_div(Cs, nw * 32);
+  if (ch == 3) ch = 4;
+  P.mt = M;
+  P.ch = ch;
+  P.r = (M == 1) ? (ch == 4 ? 2 : 4) : 2;
+  P.threads = nw * 32;
+  if (!lbc::rows_combo(P.mt, P.ch, P.r)) return fail(LBC_ERR_PARAMS, "decode tile not compiled");
+  const int occ = rows_occupancy_cached(fmt, P.mt, P.ch, P.r, P.threads);
+  if (occ <= 0) return fail(LBC_ERR_PARAMS, "decode kernel cannot be resident on an SM");
+  P.cps = std::min((p && p->nb > 0) ? p->nb : 4, occ);
+  P.grid = std::max(1, std::min(N, di.sms * P.cps));
+  return 0;
+}
+
+int run_rows(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
+  RowsPlan P;
+  if (int rc = plan_rows(fmt, a.M, a.N, a.Kp, p, P)) return rc;
+  a.status = dev_info().status;
+  cudaError_t e = lbc::rows_launch(fmt, a, P.mt, P.ch, P.r, dim3(P.grid, 1, 1), P.threads, st);
+  if (e != cudaSuccess) return fail_cuda("decode gemv launch", e);
+  return LBC_PATH_SIMT;
+}
+
 int run_gemv(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
+  if (rows_eligible(fmt, a.M, a.Kp, p)) return run_rows(fmt, a, p, st);
   GemvPlan P;
   int rc = plan_gemv(fmt, a.M, a.N, a.Kp, p, P, meta_aligned(fmt, a), a.zeros != nullptr);
   if (rc) return rc;
@@ -263,7 +325,17 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *o
   return xq_bytes + xs_bytes + as_bytes + tc_bytes;
 }
 
-bool want_tc(const lbc_params *p) { return p && p->isa == LBC_PATH_TCGEN05; }
+// Kernel path: explicit requests are honoured; automatic selection sends one
+// or two tokens to the register-streamed decode kernel and three or more to
+// the tensor-core kernel (W4A8 from 32 tokens: below that its int32 dp4a SIMT
+// kernel is faster).
+bool want_tc(const lbc_params *p, int fmt, int M) {
+  if (p && p->isa == LBC_PATH_TCGEN05) return true;
+  const bool automatic = !p || p->isa == LBC_PATH_AUTO || p->isa >= 2;
+  if (!automatic) return false;
+  if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
+  return fmt == lbc::FMT_W4A8 ? M >= 32 : M >= 3;
+}
 
 int run_tc(lbc::TcCall c, cudaStream_t st) {
   const DevInfo di = dev_info();
@@ -313,13 +385,28 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
   if (kind < 0 || kind > 2) return fail(LBC_ERR_SHAPE, "kind must be 0 (w4a16), 1 (mxfp4) or 2 (w4a8)");
   if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
   if (int rc = device_gate()) return rc;
-  GemvPlan P;
   const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
+  if (want_tc(p, fmt, M)) {
+    if (buf && buflen > 0)
+      snprintf(buf, (size_t)buflen, "{\"path\": \"tcgen05\", \"kernel\": \"tcgemm\"}");
+    return LBC_PATH_TCGEN05;
+  }
+  if (rows_eligible(fmt, M, Kp, p)) {
+    RowsPlan R;
+    if (int rc = plan_rows(fmt, M, N, Kp, p, R)) return rc;
+    if (buf && buflen > 0)
+      snprintf(buf, (size_t)buflen,
+               "{\"path\": \"simt\", \"kernel\": \"rows\", \"mt\": %d, \"ch\": %d, \"r\": %d, "
+               "\"threads\": %d, \"grid\": %d, \"ctas_per_sm\": %d}",
+               R.mt, R.ch, R.r, R.threads, R.grid, R.cps);
+    return LBC_PATH_SIMT;
+  }
+  GemvPlan P;
   const int rc = plan_gemv(fmt, M, N, Kp, p, P, true, kind != 1);
   if (rc) return rc;
   if (buf && buflen > 0)
     snprintf(buf, (size_t)buflen,
-             "{\"path\": \"simt\", \"mt\": %d, \"ch\": %d, \"rt\": %d, \"tpr\": %d, \"nt\": %d, "
+             "{\"path\": \"simt\", \"kernel\": \"staged\", \"mt\": %d, \"ch\": %d, \"rt\": %d, \"tpr\": %d, \"nt\": %d, "
              "\"tile_rows\": %d, \"stages\": %d, \"nsplit\": %d, \"seg\": %d, \"ctas_per_split\": %d, "
              "\"ntiles\": %d, \"passes\": %d, \"threads\": %d, \"smem\": %d, \"meta_tma\": %d}",
              P.mt, P.ch, P.rt, P.tpr, P.nt, P.tile_rows, P.stages, P.nsplit, P.seg, P.ctas_per_split,
@@ -333,7 +420,7 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
-  if (want_tc(p)) {
+  if (want_tc(p, lbc::FMT_W4A16, M)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A16; c.x = x; c.qw = qw; c.scales = scales; c.zeros = zeros; c.y = y;
     c.M = M; c.N = N; c.Kp = Kp;
@@ -351,7 +438,7 @@ int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8
   if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
-  if (want_tc(p)) {
+  if (want_tc(p, lbc::FMT_MXFP4, M)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_MXFP4; c.x = x; c.qw = qw; c.e8m0 = e8m0; c.y = y;
     c.M = M; c.N = N; c.Kp = Kp;
@@ -381,7 +468,7 @@ int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int 
   if (!xq || !xs || !asum || !qw || !scales || !y || !al16(xq) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
-  if (want_tc(p)) {
+  if (want_tc(p, lbc::FMT_W4A8, M)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
@@ -427,7 +514,7 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
   int rc = 0;
   cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, st);
   if (e != cudaSuccess) rc = fail_cuda("quant_act_int8 launch", e);
-  if (rc == 0 && want_tc(p)) {
+  if (rc == 0 && want_tc(p, lbc::FMT_W4A8, M)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;

@@ -32,6 +32,9 @@ namespace lbc {
 
 enum : int { FMT_W4A16 = 0, FMT_MXFP4 = 1, FMT_W4A8 = 2 };
 
+// largest row team of the register-streamed decode kernel (gemv_rows.cuh)
+constexpr int ROWS_MAX_WARPS = 8;
+
 struct GemvArgs {
   const float *x;       // [M, Kp] fp32 (W4A16 / MXFP4)
   const int8_t *xq;     // [M, Kp] int8 (W4A8)
@@ -208,8 +211,9 @@ __device__ __forceinline__ void dot_w4a16(const uint4 wv, uint32_t z, const uint
 // 2 * sum e2m1(q) * x (the caller's block scale carries the factor 1/2).
 // Codes are mapped through two 8-entry byte tables (prmt) to 16 + 2*e2m1(q),
 // a value in [4, 28], then to fp32 with the 2^23 magic number.
-template <int MT>
-__device__ __forceinline__ void dot_mxfp4(const uint4 wv, const uint64_t (*xr)[16], float (&dot)[MT],
+// xr[t][off + j] = (x[lo + j], x[hi + j]) for token t.
+template <int MT, int XN>
+__device__ __forceinline__ void dot_mxfp4(const uint4 wv, const uint64_t (*xr)[XN], int off, float (&dot)[MT],
                                           const uint32_t MAGIC) {
   const uint32_t TP0 = 0x13121110u, TP1 = 0x1C181614u;  // 16 + {0,1,2,3}, 16 + {4,6,8,12}
   const uint32_t TN0 = 0x0D0E0F10u, TN1 = 0x04080A0Cu;  // 16 - {0,1,2,3}, 16 - {4,6,8,12}
@@ -244,8 +248,8 @@ __device__ __forceinline__ void dot_mxfp4(const uint4 wv, const uint64_t (*xr)[1
           : "r"(val), "r"(MAGIC), "l"(NB));
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        accA[t] = ffma2(p0, xr[t][4 * q + 2 * half + 0], accA[t]);
-        accB[t] = ffma2(p1, xr[t][4 * q + 2 * half + 1], accB[t]);
+        accA[t] = ffma2(p0, xr[t][off + 4 * q + 2 * half + 0], accA[t]);
+        accB[t] = ffma2(p1, xr[t][off + 4 * q + 2 * half + 1], accB[t]);
       }
     }
   }
@@ -510,7 +514,7 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
           if (FMT == FMT_W4A16)
             dot_w4a16<MT>(wv, zz[j][i], xr[i], dot, MAG);
           else
-            dot_mxfp4<MT>(wv, xr[i], dot, MAG);
+            dot_mxfp4<MT, 16>(wv, xr[i], 0, dot, MAG);
 #pragma unroll
           for (int t = 0; t < MT; ++t) part[j][t] = fmaf(dot[t], sc[j][i], part[j][t]);
         }

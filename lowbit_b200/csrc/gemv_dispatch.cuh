@@ -21,6 +21,14 @@ cudaError_t gemv_launch(const GemvArgs &a, int mt, int ch, int rt, dim3 grid, in
 template <int FMT>
 int gemv_occupancy(int mt, int ch, int rt, int threads, int smem);
 
+// Register-streamed decode kernel (gemv_rows.cuh): whether (mt, ch, r) is
+// instantiated, its launch (threads = 32 * warps, grid.y = passes) and its
+// resident CTAs per SM at a block size (0 when not instantiated).
+bool rows_combo(int mt, int ch, int r);
+cudaError_t rows_launch(int fmt, const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads,
+                        cudaStream_t st);
+int rows_occupancy(int fmt, int mt, int ch, int r, int threads);
+
 // thread-local note describing the last zero-occupancy configuration
 inline char *occ_note() {
   static thread_local char buf[160] = "";

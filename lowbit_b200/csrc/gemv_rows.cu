@@ -1,0 +1,85 @@
+// gemv_rows_kernel instantiations and launch (see gemv_rows.cuh).
+#include <atomic>
+
+#include "gemv_dispatch.cuh"
+#include "gemv_rows.cuh"
+
+namespace lbc {
+
+namespace {
+
+// (MT, CH, R) combinations: MT tokens per pass, CH chunks per thread, R rows per block
+#define LBC_ROWS_COMBOS(X) X(1, 1, 4) X(1, 2, 4) X(1, 4, 2) X(2, 1, 2) X(2, 2, 2)
+
+template <int FMT, int MT, int CH, int R>
+cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_rows_kernel<FMT, MT, CH, R>, a);
+}
+
+template <int FMT, int MT, int CH, int R>
+int rows_occ_one(int threads) {
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_rows_kernel<FMT, MT, CH, R>, threads, 0) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return nb;
+}
+
+template <int FMT>
+cudaError_t rows_launch_fmt(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads, cudaStream_t st) {
+#define LBC_ROWS_L(MT, CH, R) \
+  if (mt == MT && ch == CH && r == R) return rows_launch_one<FMT, MT, CH, R>(a, grid, threads, st);
+  LBC_ROWS_COMBOS(LBC_ROWS_L)
+#undef LBC_ROWS_L
+  return cudaErrorInvalidConfiguration;
+}
+
+template <int FMT>
+int rows_occ_fmt(int mt, int ch, int r, int threads) {
+#define LBC_ROWS_O(MT, CH, R) \
+  if (mt == MT && ch == CH && r == R) return rows_occ_one<FMT, MT, CH, R>(threads);
+  LBC_ROWS_COMBOS(LBC_ROWS_O)
+#undef LBC_ROWS_O
+  return 0;
+}
+
+}  // namespace
+
+bool rows_combo(int mt, int ch, int r) {
+#define LBC_ROWS_C(MT, CH, R) \
+  if (mt == MT && ch == CH && r == R) return true;
+  LBC_ROWS_COMBOS(LBC_ROWS_C)
+#undef LBC_ROWS_C
+  return false;
+}
+
+cudaError_t rows_launch(int fmt, const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads,
+                        cudaStream_t st) {
+  switch (fmt) {
+    case FMT_W4A16: return rows_launch_fmt<FMT_W4A16>(a, mt, ch, r, grid, threads, st);
+    case FMT_MXFP4: return rows_launch_fmt<FMT_MXFP4>(a, mt, ch, r, grid, threads, st);
+    default: return rows_launch_fmt<FMT_W4A8>(a, mt, ch, r, grid, threads, st);
+  }
+}
+
+int rows_occupancy(int fmt, int mt, int ch, int r, int threads) {
+  switch (fmt) {
+    case FMT_W4A16: return rows_occ_fmt<FMT_W4A16>(mt, ch, r, threads);
+    case FMT_MXFP4: return rows_occ_fmt<FMT_MXFP4>(mt, ch, r, threads);
+    default: return rows_occ_fmt<FMT_W4A8>(mt, ch, r, threads);
+  }
+}
+
+}  // namespace lbc

@@ -1,0 +1,231 @@
+// Register-streamed decode GEMV for one or two tokens per pass.
+//
+// One CTA = one row team of NW warps (NW * 32 * CH >= Kp / 32, NW <= 8):
+// thread t owns the 16-byte chunks c = t + i*NW*32 (i < CH) of every weight
+// row, so its activations stay in registers for the whole kernel. The CTA
+// walks a contiguous range of rows (ranges differ by at most one row across
+// the grid) in blocks of R rows: each thread loads its chunks of the R rows
+// straight from HBM into registers (ld.global.nc, no L1 allocation, L2
+// evict-first), the loads of block b+1 in flight while block b is decoded --
+// no shared-memory staging, no mbarriers and no producer thread between HBM
+// and the FMA pipes. The R x MT partial dot products are reduced over the
+// team with a transposing warp reduction and one named barrier per block.
+//
+// Arithmetic per chunk is the SIMT kernel's (gemv.cuh): exact (q - z) * 2^p
+// through the 2^23 magic number and packed fp32x2 FMAs (W4A16), byte tables
+// for E2M1 (MXFP4), dp4a with -z * asum once per group (W4A8) -- the
+// reference's arithmetic (src/lowbit/csrc/kern_scalar.c:22-59) to the same
+// rounding bound.
+#pragma once
+
+#include "gemv.cuh"
+
+namespace lbc {
+
+// 16 bytes of streamed weights: read-only path, no L1 allocation, L2 evict-first
+__device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t pol) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+template <int FMT, int MT, int CH, int R>
+__global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const GemvArgs a) {
+  constexpr int V = R * MT;
+  static_assert(V <= 32 && (V & (V - 1)) == 0, "R*MT must be a power of two <= 32");
+  __shared__ float red[2][ROWS_MAX_WARPS][V];
+
+  const int NT = blockDim.x, NW = NT >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int m0 = blockIdx.y * MT;
+  const int G = a.Kp >> 7, NB32 = a.Kp >> 5, Cs = a.Kp >> 5, RB = a.Kp >> 1;
+  const int r_begin = (int)((long long)blockIdx.x * a.N / gridDim.x);
+  const int r_end = (int)((long long)(blockIdx.x + 1) * a.N / gridDim.x);
+  const int nrows = r_end - r_begin;
+  const int nblk = (nrows + R - 1) / R;
+  const bool has_z = (FMT != FMT_MXFP4) && a.zeros != nullptr;
+
+  // chunk bookkeeping; a chunk past the row end is clamped onto the last real
+  // chunk and meets zero activations, so it adds exactly 0
+  int ch_c[CH];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) ch_c[i] = min(tid + i * NT, Cs - 1);
+
+  // per-row base pointers of this CTA's first row; row rr adds rr * stride
+  const uint8_t *qbase = a.qw + (size_t)r_begin * RB;
+  const float *sbase = (FMT != FMT_MXFP4) ? a.scales + (size_t)r_begin * G : nullptr;
+  const uint8_t *zbase = has_z ? a.zeros + (size_t)r_begin * G : nullptr;
+  const uint8_t *ebase = (FMT == FMT_MXFP4) ? a.e8m0 + (size_t)r_begin * NB32 : nullptr;
+
+  const uint64_t pol = policy_evict_first();
+  uint4 w[2][R][CH];
+  float sc[2][R][CH];
+  uint32_t zz[2][R][CH];
+  (void)zz;
+  auto load = [&](int b, int buf) {
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int rr = b * R + j;
+      if (rr < nrows) {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          w[buf][j][i] = ldg_stream(qbase + (size_t)rr * RB + (ch_c[i] << 4), pol);
+          if (FMT == FMT_MXFP4) {
+            sc[buf][j][i] = e8m0_half_scale(__ldg(ebase + (size_t)rr * NB32 + ch_c[i]));
+          } else {
+            sc[buf][j][i] = __ldg(sbase + (size_t)rr * G + (ch_c[i] >> 2));
+            zz[buf][j][i] = has_z ? (uint32_t)__ldg(zbase + (size_t)rr * G + (ch_c[i] >> 2)) : 8u;
+          }
+        }
+      }
+    }
+  };
+
+  // weights are static: the first block streams before the previous kernel
+  // (which may produce X) has finished
+  if (nblk > 0) load(0, 0);
+  pdl_launch_dependents();
+  pdl_wait_prior_grid();
+
+  uint64_t xr[CH][MT][16];
+  uint32_t xl[CH][MT][4], xh[CH][MT][4];
+  int xsum[CH][MT];
+  (void)xr;
+  (void)xl;
+  (void)xh;
+  (void)xsum;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const int c = tid + i * NT;
+    int lo, hi;
+    if (FMT == FMT_MXFP4) {
+      lo = c << 5;
+      hi = lo + 16;
+    } else {
+      lo = ((c >> 2) << 7) + ((c & 3) << 4);
+      hi = lo + 64;
+    }
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const int m = m0 + t;
+      const bool ok = (c < Cs) && (m < a.M);
+      if (FMT == FMT_W4A8) {
+        uint4 vl = make_uint4(0, 0, 0, 0), vh = make_uint4(0, 0, 0, 0);
+        if (ok) {
+          vl = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + lo));
+          vh = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + hi));
+        }
+        xl[i][t][0] = vl.x; xl[i][t][1] = vl.y; xl[i][t][2] = vl.z; xl[i][t][3] = vl.w;
+        xh[i][t][0] = vh.x; xh[i][t][1] = vh.y; xh[i][t][2] = vh.z; xh[i][t][3] = vh.w;
+        // z * asum[m,g] is subtracted once per group, in its first chunk, as
+        // the reference applies it (src/lowbit/csrc/kern_scalar.c:49-59)
+        xsum[i][t] = (ok && (c & 3) == 0) ? __ldg(a.asum + (size_t)m * G + (c >> 2)) : 0;
+      } else {
+        const float4 *pl = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + lo);
+        const float4 *ph = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + hi);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f), h4 = l4;
+          if (ok) {
+            l4 = __ldg(pl + q);
+            h4 = __ldg(ph + q);
+          }
+          xr[i][t][4 * q + 0] = pack2(__float_as_uint(l4.x), __float_as_uint(h4.x));
+          xr[i][t][4 * q + 1] = pack2(__float_as_uint(l4.y), __float_as_uint(h4.y));
+          xr[i][t][4 * q + 2] = pack2(__float_as_uint(l4.z), __float_as_uint(h4.z));
+          xr[i][t][4 * q + 3] = pack2(__float_as_uint(l4.w), __float_as_uint(h4.w));
+        }
+      }
+    }
+  }
+  float xsc[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) xsc[t] = (FMT == FMT_W4A8 && m0 + t < a.M) ? __ldg(a.xs + m0 + t) : 1.f;
+  const uint32_t MAG = opaque(0x4B000000u);
+
+  auto compute = [&](int b, int buf) {
+    float part[R][MT];
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) part[j][t] = 0.f;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        const uint4 wv = w[buf][j][i];
+        if (FMT == FMT_W4A8) {
+          int acc[MT];
+#pragma unroll
+          for (int t = 0; t < MT; ++t) acc[t] = 0;
+          const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t lo = w4[q] & 0x0F0F0F0Fu;
+            const uint32_t hi = (w4[q] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+              acc[t] = dp4a_us(lo, xl[i][t][q], acc[t]);
+              acc[t] = dp4a_us(hi, xh[i][t][q], acc[t]);
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            const int d = acc[t] - (int)zz[buf][j][i] * xsum[i][t];
+            part[j][t] = fmaf((float)d, sc[buf][j][i], part[j][t]);
+          }
+        } else {
+          float dot[MT];
+          if (FMT == FMT_W4A16)
+            dot_w4a16<MT>(wv, zz[buf][j][i], xr[i], dot, MAG);
+          else
+            dot_mxfp4<MT, 16>(wv, xr[i], 0, dot, MAG);
+#pragma unroll
+          for (int t = 0; t < MT; ++t) part[j][t] = fmaf(dot[t], sc[buf][j][i], part[j][t]);
+        }
+      }
+    }
+    float v[V];
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+#pragma unroll
+      for (int t = 0; t < MT; ++t) v[j * MT + t] = part[j][t];
+    const float tot = warp_reduce_multi<V>(v, lane);
+    constexpr int PER = 32 / V;
+    int idx = -1;
+    float val = 0.f;
+    if (NW == 1) {
+      if ((lane % PER) == 0) {
+        idx = lane / PER;
+        val = tot;
+      }
+    } else {
+      if ((lane % PER) == 0) red[b & 1][warp][lane / PER] = tot;
+      named_bar_sync(1, NT);
+      if (tid < V) {
+        float s = 0.f;
+        for (int ww = 0; ww < NW; ++ww) s += red[b & 1][ww][tid];
+        idx = tid;
+        val = s;
+      }
+    }
+    if (idx >= 0) {
+      const int j = idx / MT, t = idx % MT;
+      const int rr = b * R + j, m = m0 + t;
+      if (rr < nrows && m < a.M) a.y[(size_t)m * a.N + r_begin + rr] = (FMT == FMT_W4A8) ? val * xsc[t] : val;
+    }
+  };
+
+  for (int b = 0; b < nblk; b += 2) {
+    if (b + 1 < nblk) load(b + 1, 1);
+    compute(b, 0);
+    if (b + 1 < nblk) {
+      if (b + 2 < nblk) load(b + 2, 0);
+      compute(b + 1, 1);
+    }
+  }
+}
+
+}  // namespace lbc

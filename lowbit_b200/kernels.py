@@ -10,9 +10,11 @@ error behaviour) with the computation on the GPU:
   torch CUDA tensors;
 * ``params`` is a :class:`Params` (fields reinterpreted for the GPU, see
   include/lowbit_b200.h), ``None`` or ``"auto"`` (tuned cache, lowbit_b200.tune);
-* ``isa`` selects the kernel path: None/"auto" (M <= 16 SIMT fp32, larger M
-  the tensor-core path when available), "simt", "tcgen05"; the reference's CPU
-  ISA names ("scalar", "avx2", "avx512") are accepted and mean "auto";
+* ``isa`` selects the kernel path: None/"auto" (one or two tokens: the SIMT
+  decode kernels; more: the tcgen05 tensor-core kernel,
+  for W4A8 from 32 tokens), "simt", "tcgen05"; the reference's CPU ISA names
+  ("scalar", "avx2", "avx512") are accepted and mean "auto". Explicit tiling
+  fields in ``params`` (mr, nr, nb, kb, order) keep "auto" on the SIMT kernels;
 * ``threads`` is accepted and ignored (CPU thread count).
 
 A negative return code raises ValueError for shape/parameter errors (as the
@@ -130,10 +132,10 @@ def _path_id(isa) -> int:
 
 
 def effective_isa(kind: str, isa=None, m: int = 1) -> str:
-    """Kernel path a GEMM of `kind` with `m` tokens runs on."""
+    """Kernel path a GEMM of `kind` with `m` tokens and default params runs on."""
     pid = _path_id(isa)
     if pid == -1:
-        pid = 0
+        pid = 1 if m >= (32 if kind == "w4a8" else 3) else 0
     return PATHS[pid]
 
 
