@@ -13,13 +13,12 @@ namespace lbc {
 
 namespace {
 
-int tc_mt(int M) { return M <= 4 ? 4 : (M <= 8 ? 8 : 16); }
+int tc_mt(int M) { return M == 1 ? 1 : M == 2 ? 2 : M <= 4 ? 4 : (M <= 8 ? 8 : 16); }
 int tc_npiece(int fmt) { return fmt == FMT_W4A8 ? 1 : 3; }
 int tc_bblock(int fmt, int mt) { return tc_nmma(mt, tc_npiece(fmt)) * 256 * (fmt == FMT_W4A8 ? 1 : 2); }
 
-// B blocks come from a preparation kernel (TMA-fed) for 8 or more tokens per
-// chunk; with 4 the row warps build them in shared memory.
-bool tc_btma(int mt) { return mt > 4; }
+// B blocks come from a preparation kernel and arrive by TMA with the weights.
+bool tc_btma(int) { return true; }
 
 size_t round256(size_t b) { return (b + 255) / 256 * 256; }
 
@@ -89,9 +88,11 @@ template <int FMT, int NP>
 cudaError_t dispatch_mt(int mt, const CUtensorMap &map, const TcArgs &a, int chunks, int grid_x, int smem,
                         cudaStream_t st) {
   switch (mt) {
-    case 4: return tc_launch_one<FMT, 4, NP, false>(map, a, chunks, grid_x, smem, st);
-    case 8: return tc_launch_one<FMT, 8, NP, true>(map, a, chunks, grid_x, smem, st);
-    default: return tc_launch_one<FMT, 16, NP, true>(map, a, chunks, grid_x, smem, st);
+    case 1: return tc_launch_one<FMT, 1, NP>(map, a, chunks, grid_x, smem, st);
+    case 2: return tc_launch_one<FMT, 2, NP>(map, a, chunks, grid_x, smem, st);
+    case 4: return tc_launch_one<FMT, 4, NP>(map, a, chunks, grid_x, smem, st);
+    case 8: return tc_launch_one<FMT, 8, NP>(map, a, chunks, grid_x, smem, st);
+    default: return tc_launch_one<FMT, 16, NP>(map, a, chunks, grid_x, smem, st);
   }
 }
 
@@ -123,7 +124,7 @@ int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   a.b_block_bytes = bbytes;
   a.status = c.status;
   a.epoch = next_epoch();
-  int stages = 6;
+  int stages = 8;
   while (stages > 2 && tc_smem_layout(stages, bbytes, mt).total > c.smem_optin) --stages;
   a.stages = stages;
   const int smem = tc_smem_layout(stages, bbytes, mt).total;
@@ -161,7 +162,7 @@ int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
     e = dispatch_mt<FMT_W4A8, 1>(mt, map, a, chunks, grid_x, smem, st);
   if (owned) cudaFreeAsync(scr, st);
   if (e != cudaSuccess) {
-    snprintf(err, errlen, "tensor-core GEMM launch: %s", cudaGetErrorString(e));
+    snprintf(err, errlen, "tensor-core GEMM launch: %s%s", cudaGetErrorString(e), tc_launch_note());
     return LBC_ERR_CUDA;
   }
   return LBC_PATH_TCGEN05;

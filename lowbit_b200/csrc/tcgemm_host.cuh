@@ -3,6 +3,8 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdio>
+
 #include "tcgemm.cuh"
 
 namespace lbc {
@@ -28,6 +30,12 @@ inline cudaError_t make_weight_map(CUtensorMap *map, const uint8_t *qw, int N, i
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// detail appended to launch errors (thread-local)
+inline char *tc_launch_note() {
+  static thread_local char buf[160] = "";
+  return buf;
+}
+
 template <typename Kern, typename... Args>
 inline cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -43,16 +51,16 @@ inline cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-template <int FMT, int MT, int NPIECE, bool BTMA>
+template <int FMT, int MT, int NPIECE>
 cudaError_t tc_launch_one(const CUtensorMap &map, const TcArgs &a, int chunks, int grid_x, int smem,
                           cudaStream_t st) {
-  if (BTMA) {
+  {
     cudaError_t e = launch_pdl(tc_bblock_kernel<FMT, MT, NPIECE>, dim3(a.nkb, chunks, 1), dim3(256, 1, 1),
                                (size_t)0, st, a.x, a.xq, const_cast<uint8_t *>(a.bglob), a.M, a.Kp, a.nkb,
                                a.b_block_bytes);
     if (e != cudaSuccess) return e;
   }
-  auto k = tcgemm_kernel<FMT, MT, NPIECE, BTMA>;
+  auto k = tcgemm_kernel<FMT, MT, NPIECE>;
   static int enabled[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -61,7 +69,14 @@ cudaError_t tc_launch_one(const CUtensorMap &map, const TcArgs &a, int chunks, i
     if (e != cudaSuccess) return e;
     enabled[dev] = smem;
   }
-  return launch_pdl(k, dim3(grid_x, chunks, 1), dim3(TC_THREADS, 1, 1), (size_t)smem, st, map, a);
+  cudaError_t e = launch_pdl(k, dim3(grid_x, chunks, 1), dim3(TC_THREADS, 1, 1), (size_t)smem, st, map, a);
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, k) == cudaSuccess)
+      snprintf(tc_launch_note(), 160, " [regs=%d maxThreadsPerBlock=%d smem=%d stages=%d]", fa.numRegs,
+               fa.maxThreadsPerBlock, smem, a.stages);
+  }
+  return e;
 }
 
 }  // namespace lbc
