@@ -337,6 +337,12 @@ bool want_tc(const lbc_params *p, int fmt, int M) {
   return fmt == lbc::FMT_W4A8 ? M >= 32 : M >= 3;
 }
 
+// bf16 prefill kernel (4e-3 tolerance, the north-star prefill contract) from
+// 64 tokens unless tokens per pass (mr) are given, which keeps the exact kernel
+bool want_prefill(const lbc_params *p, int fmt, int M) {
+  return fmt != lbc::FMT_W4A8 && M >= 64 && !(p && p->mr > 0);
+}
+
 int run_tc(lbc::TcCall c, cudaStream_t st) {
   const DevInfo di = dev_info();
   c.status = di.status;
@@ -388,7 +394,8 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
   const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
   if (want_tc(p, fmt, M)) {
     if (buf && buflen > 0)
-      snprintf(buf, (size_t)buflen, "{\"path\": \"tcgen05\", \"kernel\": \"tcgemm\"}");
+      snprintf(buf, (size_t)buflen, "{\"path\": \"tcgen05\", \"kernel\": \"%s\"}",
+               want_prefill(p, fmt, M) ? "prefill" : "tcgemm");
     return LBC_PATH_TCGEN05;
   }
   if (rows_eligible(fmt, M, Kp, p)) {
@@ -424,6 +431,7 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A16; c.x = x; c.qw = qw; c.scales = scales; c.zeros = zeros; c.y = y;
     c.M = M; c.N = N; c.Kp = Kp;
+    c.prefill = want_prefill(p, c.fmt, M);
     return run_tc(c, static_cast<cudaStream_t>(stream));
   }
   lbc::GemvArgs a{};
@@ -442,6 +450,7 @@ int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8
     lbc::TcCall c{};
     c.fmt = lbc::FMT_MXFP4; c.x = x; c.qw = qw; c.e8m0 = e8m0; c.y = y;
     c.M = M; c.N = N; c.Kp = Kp;
+    c.prefill = want_prefill(p, c.fmt, M);
     return run_tc(c, static_cast<cudaStream_t>(stream));
   }
   lbc::GemvArgs a{};

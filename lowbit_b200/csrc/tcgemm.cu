@@ -100,7 +100,64 @@ cudaError_t dispatch_mt(int mt, const CUtensorMap &map, const TcArgs &a, int chu
 
 size_t tc_scratch_bytes(int fmt, int M, int Kp, int ctas) { return scratch_bytes(fmt, M, Kp, ctas); }
 
+namespace {
+
+// Prefill: activation blocks [token chunks][K blocks][128 rows x 256 K bf16]
+// in the scratch, then the prefill kernel over (128-row, 128-token) tiles.
+int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
+  const int fmt = c.fmt;
+  TcArgs a{};
+  a.x = c.x;
+  a.scales = c.scales;
+  a.zeros = c.zeros;
+  a.e8m0 = c.e8m0;
+  a.y = c.y;
+  a.M = c.M;
+  a.N = c.N;
+  a.Kp = c.Kp;
+  a.G = c.Kp / 128;
+  a.nkb = (c.Kp + 255) / 256;
+  a.ntiles = (c.N + TC_ROWS - 1) / TC_ROWS;
+  const int nch = (c.M + PF_TOK - 1) / PF_TOK;
+  a.units = a.ntiles * nch;
+  a.b_block_bytes = tc_nmma(PF_TOK, 1) * 256 * 2;
+  a.status = c.status;
+  int stages = 4;
+  while (stages > 2 && tc_smem_layout(stages, a.b_block_bytes, PF_TOK).total > c.smem_optin) --stages;
+  a.stages = stages;
+  const int smem = tc_smem_layout(stages, a.b_block_bytes, PF_TOK).total;
+  if (smem > c.smem_optin) {
+    snprintf(err, errlen, "prefill tile does not fit in shared memory");
+    return LBC_ERR_PARAMS;
+  }
+  const int grid_x = a.units < c.sms ? a.units : c.sms;
+  CUtensorMap map;
+  if (make_weight_map(&map, c.qw, c.N, c.Kp) != cudaSuccess) {
+    snprintf(err, errlen, "cuTensorMapEncodeTiled failed for the weight tensor");
+    return LBC_ERR_CUDA;
+  }
+  const size_t need = round256((size_t)nch * a.nkb * a.b_block_bytes);
+  bool owned = false;
+  uint8_t *scr = static_cast<uint8_t *>(cached_scratch(need, st, &owned));
+  if (!scr) {
+    snprintf(err, errlen, "allocation of %zu bytes of GEMM scratch failed", need);
+    return LBC_ERR_ALLOC;
+  }
+  a.bglob = scr;
+  cudaError_t e = fmt == FMT_W4A16 ? tc_prefill_launch<FMT_W4A16>(map, a, nch, grid_x, smem, st)
+                                   : tc_prefill_launch<FMT_MXFP4>(map, a, nch, grid_x, smem, st);
+  if (owned) cudaFreeAsync(scr, st);
+  if (e != cudaSuccess) {
+    snprintf(err, errlen, "tensor-core prefill launch: %s%s", cudaGetErrorString(e), tc_launch_note());
+    return LBC_ERR_CUDA;
+  }
+  return LBC_PATH_TCGEN05;
+}
+
+}  // namespace
+
 int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
+  if (c.prefill && c.fmt != FMT_W4A8) return tc_prefill(c, st, err, errlen);
   const int fmt = c.fmt;
   const int mt = tc_mt(c.M);
   const int chunks = (c.M + mt - 1) / mt;

@@ -5,7 +5,7 @@
 
 #include <cstdio>
 
-#include "tcgemm.cuh"
+#include "tcprefill.cuh"
 
 namespace lbc {
 
@@ -74,6 +74,36 @@ cudaError_t tc_launch_one(const CUtensorMap &map, const TcArgs &a, int chunks, i
     cudaFuncAttributes fa{};
     if (cudaFuncGetAttributes(&fa, k) == cudaSuccess)
       snprintf(tc_launch_note(), 160, " [regs=%d maxThreadsPerBlock=%d smem=%d stages=%d]", fa.numRegs,
+               fa.maxThreadsPerBlock, smem, a.stages);
+  }
+  return e;
+}
+
+}  // namespace lbc
+
+namespace lbc {
+
+template <int FMT>
+cudaError_t tc_prefill_launch(const CUtensorMap &map, const TcArgs &a, int nch, int grid_x, int smem, cudaStream_t st) {
+  {
+    cudaError_t e = launch_pdl(tc_bblock_kernel<FMT, PF_TOK, 1>, dim3(a.nkb, nch, 1), dim3(256, 1, 1), (size_t)0,
+                               st, a.x, a.xq, const_cast<uint8_t *>(a.bglob), a.M, a.Kp, a.nkb, a.b_block_bytes);
+    if (e != cudaSuccess) return e;
+  }
+  auto k = tcprefill_kernel<FMT>;
+  static int enabled[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && enabled[dev] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    enabled[dev] = smem;
+  }
+  cudaError_t e = launch_pdl(k, dim3(grid_x, 1, 1), dim3(PF_THREADS, 1, 1), (size_t)smem, st, map, a);
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, k) == cudaSuccess)
+      snprintf(tc_launch_note(), 160, " [prefill regs=%d maxThreadsPerBlock=%d smem=%d stages=%d]", fa.numRegs,
                fa.maxThreadsPerBlock, smem, a.stages);
   }
   return e;
