@@ -704,13 +704,13 @@ __global__ void __maxnreg__(80) tcgemm_kernel(const __grid_constant__ CUtensorMa
 // the permuted K order and canonical K-major layout the MMA reads, rows
 // n = piece*MT + token, absent tokens / pieces / K positions zero. One CTA per
 // block; each thread writes whole 16-byte rows (8 bf16 or 16 int8 values).
-template <int FMT, int MT, int NPIECE>
+template <int FMT, int MT, int NPIECE, int KBLK = TC_KB>
 __global__ void __launch_bounds__(256) tc_bblock_kernel(const float *__restrict__ x, const int8_t *__restrict__ xq,
                                                         uint8_t *__restrict__ out, int M, int Kp, int nkb,
                                                         int bbytes) {
   constexpr bool I8 = (FMT == FMT_W4A8);
-  constexpr int SBO = I8 ? 2048 : 4096;
-  constexpr int EPR = I8 ? 16 : 8;  // elements per 16-byte row
+  constexpr int SBO = KBLK / (I8 ? 16 : 8) * 128;  // bytes between 8-row groups
+  constexpr int EPR = I8 ? 16 : 8;                  // elements per 16-byte row
   const int kb = blockIdx.x, chunk = blockIdx.y;
   uint8_t *blk = out + ((size_t)chunk * nkb + kb) * bbytes;
   pdl_wait_prior_grid();
@@ -726,7 +726,7 @@ __global__ void __launch_bounds__(256) tc_bblock_kernel(const float *__restrict_
 #pragma unroll
       for (int e = 0; e < EPR; ++e) {
         const int kk = kk0 + e;
-        const int k = kb * TC_KB + (kk >> 7) * 128 + tc_perm(FMT, kk & 127);
+        const int k = kb * KBLK + (kk >> 7) * 128 + tc_perm(FMT, kk & 127);
         if (k < Kp) {
           if (I8) {
             w[e >> 2] |= (uint32_t)(uint8_t)xq[(size_t)m * Kp + k] << (8 * (e & 3));
