@@ -226,15 +226,24 @@ def run_ours(args) -> dict | None:
     pool_mb = copies * wbytes_local / 2**20
     xd = torch.from_numpy(x).to(dev)
     prep = Kn._Prepared(xd, W.kp, n_loc)
-    yfull = torch.empty((world, M, n_loc), dtype=torch.float32, device=dev)
+    cp = fused = None
+    if world > 1:
+        from lowbit_b200.sharding import ColumnParallel, FusedColumnParallel
+        cp = ColumnParallel(M, N)              # NCCL all-gather (reported beside)
+        fused = FusedColumnParallel(M, N)      # GEMV + NVLink peer-store gather in one kernel
 
     def gemv(i):
         Kn.gemm_w4a16(prep.x, pool[i % copies], _prep=prep)
 
     def step(i):
-        gemv(i)
         if world > 1:
-            dist.all_gather_into_tensor(yfull, prep.y)
+            fused(prep.x, pool[i % copies], _prep=prep)
+        else:
+            gemv(i)
+
+    def step_nccl(i):
+        gemv(i)
+        cp.gather(prep.y)
 
     def barrier():
         if world > 1:
@@ -267,6 +276,7 @@ def run_ours(args) -> dict | None:
 
     g_step = capture(step, args.steps)
     g_gemv = capture(gemv, args.steps) if world > 1 else g_step
+    g_nccl = capture(step_nccl, args.steps) if world > 1 else None
     g_step.replay()  # graph warm-up (not timed)
     torch.cuda.synchronize()
 
@@ -297,14 +307,25 @@ def run_ours(args) -> dict | None:
     ev3.record()
     torch.cuda.synchronize()
     ms_kernel_local = ev2.elapsed_time(ev3) / args.steps
+    ms_nccl_local = 0.0
+    if g_nccl is not None:
+        barrier()
+        torch.cuda.synchronize()
+        ev2.record()
+        g_nccl.replay()
+        ev3.record()
+        torch.cuda.synchronize()
+        ms_nccl_local = ev2.elapsed_time(ev3) / args.steps
     clk = clocks.stop()
 
-    t = torch.tensor([ms_step_local, ms_kernel_local], device=dev)
+    t = torch.tensor([ms_step_local, ms_kernel_local, ms_nccl_local], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step, ms_kernel = float(t[0]), float(t[1])
+    ms_step, ms_kernel, ms_nccl = float(t[0]), float(t[1]), float(t[2])
 
     # end to end through the public API, host buffers (pinned) in and out every step
+    if fused is not None:
+        fused.resync()
     xh = torch.from_numpy(x).pin_memory()
     yh = torch.empty((M, N), dtype=torch.float32).pin_memory()
     xdev = torch.empty((M, K), dtype=torch.float32, device=dev)
@@ -312,12 +333,11 @@ def run_ours(args) -> dict | None:
 
     def e2e_step(i):
         xdev.copy_(xh, non_blocking=True)
-        y = lb.gemm_w4a16(xdev, pool[i % copies])
         if world > 1:
-            dist.all_gather_into_tensor(yfull, y)
-            yh.copy_(yfull.permute(1, 0, 2).reshape(M, N), non_blocking=True)
+            y = fused(xdev, pool[i % copies])
         else:
-            yh.copy_(y, non_blocking=True)
+            y = lb.gemm_w4a16(xdev, pool[i % copies])
+        yh.copy_(y, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     for i in range(5):
@@ -332,8 +352,10 @@ def run_ours(args) -> dict | None:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_s = float(te[0])
 
-    del g_step, g_gemv
+    del g_step, g_gemv, g_nccl
     status = Kn.device_status(reset=True)
+    if fused is not None:
+        fused.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -352,7 +374,8 @@ def run_ours(args) -> dict | None:
         "vs_baseline": round(value / PUBLISHED_GBPS, 2), "dtype": "f32",
         "data": "synthetic: W~N(0,1) seed 0, X~N(0,1) seed 1, quantized by quantize_int4(asym=True)",
         "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "format": "w4a16",
-                   "parallelism": f"N-shard x{world}" + (" + NCCL all-gather of Y" if world > 1 else ""),
+                   "parallelism": f"N-shard x{world}" + (" + all-gather of Y fused into the GEMV (NVLink peer stores)"
+                                                        if world > 1 else ""),
                    "l2": f"inputs larger than L2: {copies} rotating weight copies ({pool_mb:.0f} MB/rank)",
                    "timing": "K steps in one CUDA graph replay, CUDA events, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -362,6 +385,8 @@ def run_ours(args) -> dict | None:
                 "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4,
                 "us_per_step": round(e2e_s * 1e6, 2)},
         "gpu_launches": args.steps,
+        "multi_gpu": ({"fused_step_us": round(ms_step * 1e3, 3), "gemv_only_us": round(ms_kernel * 1e3, 3),
+                       "nccl_allgather_step_us": round(ms_nccl * 1e3, 3)} if world > 1 else None),
         "clocks": clk,
         "device_status": status,
     }

@@ -166,6 +166,39 @@ int lbc_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, int Kp,
                        const uint8_t *qw, const uint8_t *zeros, int N,
                        int32_t *out, int isa, void *stream);
 
+/* ---- multi-GPU (column-parallel) decode: no reference counterpart; this is
+ * the north star's "N-sharded W with an all-gather of Y" made one kernel.
+ *
+ * Device buffers another process on the node can map (CUDA IPC): allocate
+ * with lbc_device_alloc (zero-filled, an IPC-exportable base allocation),
+ * export a handle, open the peers' handles. */
+#define LBC_IPC_HANDLE_BYTES 64
+int lbc_device_alloc(size_t bytes, void **dev_ptr);
+int lbc_device_free(void *dev_ptr);
+int lbc_ipc_get_handle(const void *dev_ptr, void *handle);
+int lbc_ipc_open_handle(const void *handle, void **dev_ptr);
+int lbc_ipc_close_handle(void *dev_ptr);
+
+/* W4A16 decode (M <= 2) of this rank's weight rows [row0, row0 + N_local) of
+ * an N_total-row matrix, with the all-gather fused in. The call's epoch is
+ * *epoch + 1 (`epoch`: this rank's zero-initialised device counter); every
+ * output value is stored into y_peers[(epoch % 2) * world + p] for every rank
+ * p (a DEVICE array of 2 * world pointers to [M, N_total] fp32 buffers: two
+ * per rank, by call parity, peer pointers opened over IPC) at row0 + n; the
+ * kernel then publishes the epoch in flag_peers[p][rank] for every p, waits
+ * (bounded: LBC_ERR_TIMEOUT in lbc_device_status) until every rank's epoch
+ * has arrived in flag_peers[rank][*], and stores it in *epoch. When the
+ * stream's work completes, Y is whole on this GPU; nothing is baked into the
+ * launch, so CUDA graphs of these calls replay correctly. `counter` is this
+ * rank's zero-initialised CTA counter (one uint32). Returns LBC_PATH_SIMT or
+ * a negative error (LBC_ERR_PARAMS for M > 2 or explicit tiling params). */
+int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw,
+                             const float *scales, const uint8_t *zeros, int N_local,
+                             int row0, int N_total, float *const *y_peers,
+                             uint32_t *const *flag_peers, uint32_t *counter,
+                             uint32_t *epoch, int rank, int world, const lbc_params *p,
+                             void *stream);
+
 #ifdef __cplusplus
 }
 #endif

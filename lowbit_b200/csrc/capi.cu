@@ -553,4 +553,78 @@ int lbc_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, int Kp, con
   return 0;
 }
 
+// ------------------------------------------------------------------ multi-GPU
+int lbc_device_alloc(size_t bytes, void **dev_ptr) {
+  if (!dev_ptr || bytes == 0) return fail(LBC_ERR_SHAPE, "bytes must be > 0 and dev_ptr non-NULL");
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LBC_ERR_ALLOC, "cudaMalloc failed");
+  }
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail_cuda("cudaMemset", e);
+  }
+  *dev_ptr = p;
+  return 0;
+}
+
+int lbc_device_free(void *dev_ptr) {
+  cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? 0 : fail_cuda("cudaFree", e);
+}
+
+int lbc_ipc_get_handle(const void *dev_ptr, void *handle) {
+  if (!dev_ptr || !handle) return fail(LBC_ERR_SHAPE, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr));
+  if (e != cudaSuccess) return fail_cuda("cudaIpcGetMemHandle", e);
+  static_assert(sizeof(h) == LBC_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof h);
+  return 0;
+}
+
+int lbc_ipc_open_handle(const void *handle, void **dev_ptr) {
+  if (!handle || !dev_ptr) return fail(LBC_ERR_SHAPE, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail_cuda("cudaIpcOpenMemHandle", e);
+  return 0;
+}
+
+int lbc_ipc_close_handle(void *dev_ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? 0 : fail_cuda("cudaIpcCloseMemHandle", e);
+}
+
+int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
+                             const uint8_t *zeros, int N_local, int row0, int N_total, float *const *y_peers,
+                             uint32_t *const *flag_peers, uint32_t *counter, uint32_t *epoch, int rank,
+                             int world, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N_local, LBC_GROUP)) return rc;
+  if (!x || !qw || !scales || !y_peers || !flag_peers || !counter || !epoch || !al16(x) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer");
+  if (world < 1 || rank < 0 || rank >= world || row0 < 0 || row0 + N_local > N_total)
+    return fail(LBC_ERR_SHAPE, "rank / world / row range out of bounds");
+  if (!rows_eligible(lbc::FMT_W4A16, M, Kp, p))
+    return fail(LBC_ERR_PARAMS, "the fused all-gather decode serves one or two tokens with default tiling");
+  if (int rc = device_gate()) return rc;
+  RowsPlan P;
+  if (int rc = plan_rows(lbc::FMT_W4A16, M, N_local, Kp, p, P)) return rc;
+  lbc::GemvArgs a{};
+  a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros;
+  a.M = M; a.N = N_local; a.Kp = Kp;
+  a.status = dev_info().status;
+  a.y_peers = y_peers; a.flag_peers = flag_peers; a.counter = counter;
+  a.epoch = epoch; a.rank = rank; a.world = world; a.row0 = row0; a.ld_y = N_total;
+  cudaError_t e = lbc::rows_gather_launch(a, P.mt, P.ch, P.r, dim3(P.grid, 1, 1), P.threads,
+                                          static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidConfiguration) return fail(LBC_ERR_PARAMS, "decode tile has no fused all-gather variant");
+  if (e != cudaSuccess) return fail_cuda("fused all-gather decode launch", e);
+  return LBC_PATH_SIMT;
+}
+
 }  // extern "C"

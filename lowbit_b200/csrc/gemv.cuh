@@ -57,6 +57,12 @@ struct GemvArgs {
   int atomic_out;       // 1: accumulate into y with atomics (split-K)
   int meta_tma;         // 1: scales/zeros/e8m0 travel with the weights in each stage
   int *status;          // device status word (bounded-wait timeouts)
+  // fused all-gather (column-parallel decode over NVLink peers), else unused:
+  float *const *y_peers;        // [2][world] Y buffers [M, ld_y] of every rank, by call parity
+  uint32_t *const *flag_peers;  // [world] flag arrays [world] of every rank
+  uint32_t *counter;            // this rank's CTA completion counter
+  uint32_t *epoch;              // this rank's call counter (the flags carry it)
+  int rank, world, row0, ld_y;  // this rank's first global row, Y row stride
 };
 
 // Per-stage metadata region (scales + zero points, or E8M0 exponents) when it

@@ -28,6 +28,9 @@ bool rows_combo(int mt, int ch, int r);
 cudaError_t rows_launch(int fmt, const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads,
                         cudaStream_t st);
 int rows_occupancy(int fmt, int mt, int ch, int r, int threads);
+// W4A16 decode with the column-parallel all-gather fused in (a.y_peers ...);
+// (mt, ch, r) in {(1,1,4), (1,2,4), (2,1,2)}
+cudaError_t rows_gather_launch(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads, cudaStream_t st);
 
 // thread-local note describing the last zero-occupancy configuration
 inline char *occ_note() {

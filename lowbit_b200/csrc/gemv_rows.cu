@@ -11,7 +11,7 @@ namespace {
 // (MT, CH, R) combinations: MT tokens per pass, CH chunks per thread, R rows per block
 #define LBC_ROWS_COMBOS(X) X(1, 1, 4) X(1, 2, 4) X(1, 4, 2) X(2, 1, 2) X(2, 2, 2)
 
-template <int FMT, int MT, int CH, int R>
+template <int FMT, int MT, int CH, int R, bool GATHER = false>
 cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -23,7 +23,7 @@ cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_rows_kernel<FMT, MT, CH, R>, a);
+  return cudaLaunchKernelEx(&cfg, gemv_rows_kernel<FMT, MT, CH, R, GATHER>, a);
 }
 
 template <int FMT, int MT, int CH, int R>
@@ -46,6 +46,15 @@ cudaError_t rows_launch_fmt(const GemvArgs &a, int mt, int ch, int r, dim3 grid,
   return cudaErrorInvalidConfiguration;
 }
 
+// fused all-gather variant (W4A16, one token, one chunk per thread)
+cudaError_t rows_gather_launch_w4a16(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads,
+                                     cudaStream_t st) {
+  if (mt == 1 && ch == 1 && r == 4) return rows_launch_one<FMT_W4A16, 1, 1, 4, true>(a, grid, threads, st);
+  if (mt == 1 && ch == 2 && r == 4) return rows_launch_one<FMT_W4A16, 1, 2, 4, true>(a, grid, threads, st);
+  if (mt == 2 && ch == 1 && r == 2) return rows_launch_one<FMT_W4A16, 2, 1, 2, true>(a, grid, threads, st);
+  return cudaErrorInvalidConfiguration;
+}
+
 template <int FMT>
 int rows_occ_fmt(int mt, int ch, int r, int threads) {
 #define LBC_ROWS_O(MT, CH, R) \
@@ -56,6 +65,10 @@ int rows_occ_fmt(int mt, int ch, int r, int threads) {
 }
 
 }  // namespace
+
+cudaError_t rows_gather_launch(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads, cudaStream_t st) {
+  return rows_gather_launch_w4a16(a, mt, ch, r, grid, threads, st);
+}
 
 bool rows_combo(int mt, int ch, int r) {
 #define LBC_ROWS_C(MT, CH, R) \

@@ -31,7 +31,32 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t pol) {
   return v;
 }
 
-template <int FMT, int MT, int CH, int R>
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t *p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// GATHER: column-parallel decode with the all-gather fused in. The call's
+// epoch is the device counter + 1 (read after griddepcontrol.wait, so a
+// launch that starts early under PDL sees the previous call's update); each
+// output value goes to this rank's rows of its epoch-parity Y buffer; the
+// last CTA to finish copies the slice into every peer's buffer (peer pointers
+// over NVLink), publishes the epoch in every rank's flag array, waits
+// (bounded) until every rank's epoch has arrived in its own, and advances the
+// counter. When the kernel
+// completes, Y is whole on this GPU. No epoch is baked into the launch, so a
+// CUDA graph of these calls replays correctly.
+template <int FMT, int MT, int CH, int R, bool GATHER = false>
 __global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const GemvArgs a) {
   constexpr int V = R * MT;
   static_assert(V <= 32 && (V & (V - 1)) == 0, "R*MT must be a power of two <= 32");
@@ -144,6 +169,13 @@ __global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const Ge
 #pragma unroll
   for (int t = 0; t < MT; ++t) xsc[t] = (FMT == FMT_W4A8 && m0 + t < a.M) ? __ldg(a.xs + m0 + t) : 1.f;
   const uint32_t MAG = opaque(0x4B000000u);
+  uint32_t epoch = 0;
+  float *const *ydst = nullptr;
+  if (GATHER) {
+    epoch = *reinterpret_cast<volatile const uint32_t *>(a.epoch) + 1u;
+    ydst = a.y_peers + (epoch & 1u) * a.world;
+  }
+  (void)ydst;
 
   auto compute = [&](int b, int buf) {
     float part[R][MT];
@@ -214,7 +246,14 @@ __global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const Ge
     if (idx >= 0) {
       const int j = idx / MT, t = idx % MT;
       const int rr = b * R + j, m = m0 + t;
-      if (rr < nrows && m < a.M) a.y[(size_t)m * a.N + r_begin + rr] = (FMT == FMT_W4A8) ? val * xsc[t] : val;
+      if (rr < nrows && m < a.M) {
+        const float out = (FMT == FMT_W4A8) ? val * xsc[t] : val;
+        if (GATHER) {
+          ydst[a.rank][(size_t)m * a.ld_y + a.row0 + r_begin + rr] = out;  // local slice first
+        } else {
+          a.y[(size_t)m * a.N + r_begin + rr] = out;
+        }
+      }
     }
   };
 
@@ -224,6 +263,57 @@ __global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const Ge
     if (b + 1 < nblk) {
       if (b + 2 < nblk) load(b + 2, 0);
       compute(b + 1, 1);
+    }
+  }
+
+  if (GATHER) {
+    __shared__ int last;
+    // the CTA's slice rows are released (bar.sync, then thread 0's release
+    // atomic, cumulative over the CTA) before it counts itself; the CTA that
+    // completes the count acquires every slice, copies the whole slice to
+    // every peer with 16-byte stores (one coalesced stream per peer), then
+    // one system-scope fence orders the copies before the epoch flags
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t total = gridDim.x * gridDim.y;
+      last = (atom_add_acq_rel_gpu(a.counter, 1u) + 1u == total) ? 1 : 0;
+      if (last) atomicExch(a.counter, 0u);  // ready for the next call
+    }
+    __syncthreads();
+    if (!last) return;
+    const int nloc = a.N;
+    for (int p = 0; p < a.world; ++p) {
+      if (p == a.rank) continue;
+      for (int m = 0; m < a.M; ++m) {
+        const float *src = ydst[a.rank] + (size_t)m * a.ld_y + a.row0;
+        float *dst = ydst[p] + (size_t)m * a.ld_y + a.row0;
+        // scalar head up to 16-byte alignment, vector body, scalar tail
+        const int head = min(nloc, (int)((16 - (reinterpret_cast<uintptr_t>(src) & 15)) & 15) / 4);
+        for (int j = tid; j < head; j += NT) dst[j] = src[j];
+        const int nvec = (nloc - head) / 4;
+        const float4 *s4 = reinterpret_cast<const float4 *>(src + head);
+        float4 *d4 = reinterpret_cast<float4 *>(dst + head);
+        for (int j = tid; j < nvec; j += NT) d4[j] = s4[j];
+        for (int j = head + 4 * nvec + tid; j < nloc; j += NT) dst[j] = src[j];
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      fence_acq_rel_sys();
+      for (int p = 0; p < a.world; ++p) st_relaxed_sys_u32(a.flag_peers[p] + a.rank, epoch);
+      // flags only grow: a rank already at a later call has also passed this one
+      const uint32_t *mine = a.flag_peers[a.rank];
+      const long long t0 = clock64();
+      for (int p = 0; p < a.world; ++p) {
+        while ((int32_t)(ld_acquire_sys_u32(mine + p) - epoch) < 0) {
+          if (clock64() - t0 > LBC_WAIT_CYCLES) {
+            set_status(a.status, LBC_ERR_TIMEOUT);
+            return;
+          }
+          __nanosleep(32);
+        }
+      }
+      *a.epoch = epoch;
     }
   }
 }

@@ -89,6 +89,13 @@ def lib() -> C.CDLL:
         "lbc_gemm_w4a8_q": ([_vp, _vp, _vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_quant_act_int8": ([_vp, _int, _int, _vp, _vp, _vp, _vp], _int),
         "lbc_w4a8_group_acc": ([_vp, _vp, _int, _int, _vp, _vp, _int, _vp, _int, _vp], _int),
+        "lbc_device_alloc": ([C.c_size_t, C.POINTER(_vp)], _int),
+        "lbc_device_free": ([_vp], _int),
+        "lbc_ipc_get_handle": ([_vp, _vp], _int),
+        "lbc_ipc_open_handle": ([_vp, C.POINTER(_vp)], _int),
+        "lbc_ipc_close_handle": ([_vp], _int),
+        "lbc_gemm_w4a16_allgather": ([_vp, _int, _int, _vp, _vp, _vp, _int, _int, _int, _vp, _vp, _vp, _vp,
+                                      _int, _int, _pp, _vp], _int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(so, name)
