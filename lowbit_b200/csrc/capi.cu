@@ -264,7 +264,8 @@ int plan_rows(int fmt, int M, int N, int Kp, const lbc_params *p, RowsPlan &P) {
   const int occ = rows_occupancy_cached(fmt, P.mt, P.ch, P.r, P.threads);
   if (occ <= 0) return fail(LBC_ERR_PARAMS, "decode kernel cannot be resident on an SM");
   P.cps = std::min((p && p->nb > 0) ? p->nb : 4, occ);
-  P.grid = std::max(1, std::min(N, di.sms * P.cps));
+  // the kernel hands out whole blocks of r rows
+  P.grid = std::max(1, std::min(ceil_div(N, P.r), di.sms * P.cps));
   return 0;
 }
 

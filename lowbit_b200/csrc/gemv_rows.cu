@@ -11,11 +11,11 @@ namespace {
 // (MT, CH, R) combinations: MT tokens per pass, CH chunks per thread, R rows per block
 #define LBC_ROWS_COMBOS(X) X(1, 1, 4) X(1, 2, 4) X(1, 4, 2) X(2, 1, 2) X(2, 2, 2)
 
-template <int FMT, int MT, int CH, int R, bool GATHER = false>
-cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStream_t st) {
+template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false>
+cudaError_t rows_launch_nw(const GemvArgs &a, dim3 grid, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.blockDim = dim3(NW * 32, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -23,18 +23,49 @@ cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStrea
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_rows_kernel<FMT, MT, CH, R, GATHER>, a);
+  return cudaLaunchKernelEx(&cfg, gemv_rows_kernel<FMT, MT, CH, R, NW, GATHER>, a);
 }
 
-template <int FMT, int MT, int CH, int R>
-int rows_occ_one(int threads) {
+// the row team is 1..ROWS_MAX_WARPS (8) warps
+template <int FMT, int MT, int CH, int R, bool GATHER = false>
+cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStream_t st) {
+  switch (threads / 32) {
+    case 1: return rows_launch_nw<FMT, MT, CH, R, 1, GATHER>(a, grid, st);
+    case 2: return rows_launch_nw<FMT, MT, CH, R, 2, GATHER>(a, grid, st);
+    case 3: return rows_launch_nw<FMT, MT, CH, R, 3, GATHER>(a, grid, st);
+    case 4: return rows_launch_nw<FMT, MT, CH, R, 4, GATHER>(a, grid, st);
+    case 5: return rows_launch_nw<FMT, MT, CH, R, 5, GATHER>(a, grid, st);
+    case 6: return rows_launch_nw<FMT, MT, CH, R, 6, GATHER>(a, grid, st);
+    case 7: return rows_launch_nw<FMT, MT, CH, R, 7, GATHER>(a, grid, st);
+    case 8: return rows_launch_nw<FMT, MT, CH, R, 8, GATHER>(a, grid, st);
+    default: return cudaErrorInvalidConfiguration;
+  }
+}
+
+template <int FMT, int MT, int CH, int R, int NW>
+int rows_occ_nw() {
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_rows_kernel<FMT, MT, CH, R>, threads, 0) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_rows_kernel<FMT, MT, CH, R, NW>, NW * 32, 0) !=
       cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return nb;
+}
+
+template <int FMT, int MT, int CH, int R>
+int rows_occ_one(int threads) {
+  switch (threads / 32) {
+    case 1: return rows_occ_nw<FMT, MT, CH, R, 1>();
+    case 2: return rows_occ_nw<FMT, MT, CH, R, 2>();
+    case 3: return rows_occ_nw<FMT, MT, CH, R, 3>();
+    case 4: return rows_occ_nw<FMT, MT, CH, R, 4>();
+    case 5: return rows_occ_nw<FMT, MT, CH, R, 5>();
+    case 6: return rows_occ_nw<FMT, MT, CH, R, 6>();
+    case 7: return rows_occ_nw<FMT, MT, CH, R, 7>();
+    case 8: return rows_occ_nw<FMT, MT, CH, R, 8>();
+    default: return 0;
+  }
 }
 
 template <int FMT>
@@ -46,7 +77,7 @@ cudaError_t rows_launch_fmt(const GemvArgs &a, int mt, int ch, int r, dim3 grid,
   return cudaErrorInvalidConfiguration;
 }
 
-// fused all-gather variant (W4A16, one token, one chunk per thread)
+// fused all-gather variant (W4A16, one or two tokens)
 cudaError_t rows_gather_launch_w4a16(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads,
                                      cudaStream_t st) {
   if (mt == 1 && ch == 1 && r == 4) return rows_launch_one<FMT_W4A16, 1, 1, 4, true>(a, grid, threads, st);

@@ -3,8 +3,8 @@
 // One CTA = one row team of NW warps (NW * 32 * CH >= Kp / 32, NW <= 8):
 // thread t owns the 16-byte chunks c = t + i*NW*32 (i < CH) of every weight
 // row, so its activations stay in registers for the whole kernel. The CTA
-// walks a contiguous range of rows (ranges differ by at most one row across
-// the grid) in blocks of R rows: each thread loads its chunks of the R rows
+// walks a contiguous range of whole blocks of R rows (block counts differ by
+// at most one across the grid): each thread loads its chunks of the R rows
 // straight from HBM into registers (ld.global.nc, no L1 allocation, L2
 // evict-first), the loads of block b+1 in flight while block b is decoded --
 // no shared-memory staging, no mbarriers and no producer thread between HBM
@@ -56,20 +56,25 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
 // counter. When the kernel
 // completes, Y is whole on this GPU. No epoch is baked into the launch, so a
 // CUDA graph of these calls replays correctly.
-template <int FMT, int MT, int CH, int R, bool GATHER = false>
-__global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const GemvArgs a) {
+template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false>
+__global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   constexpr int V = R * MT;
   static_assert(V <= 32 && (V & (V - 1)) == 0, "R*MT must be a power of two <= 32");
-  __shared__ float red[2][ROWS_MAX_WARPS][V];
+  static_assert(NW >= 1 && NW <= ROWS_MAX_WARPS, "1..ROWS_MAX_WARPS warps per row team");
+  constexpr int NT = NW * 32;
+  __shared__ float red[2][NW][V];
 
-  const int NT = blockDim.x, NW = NT >> 5;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int m0 = blockIdx.y * MT;
   const int G = a.Kp >> 7, NB32 = a.Kp >> 5, Cs = a.Kp >> 5, RB = a.Kp >> 1;
-  const int r_begin = (int)((long long)blockIdx.x * a.N / gridDim.x);
-  const int r_end = (int)((long long)(blockIdx.x + 1) * a.N / gridDim.x);
-  const int nrows = r_end - r_begin;
-  const int nblk = (nrows + R - 1) / R;
+  // whole blocks of R rows per CTA (block counts differ by at most one across
+  // the grid); only the matrix's last block can be partial
+  const int ntile = (a.N + R - 1) / R;
+  const int t_begin = (int)((long long)blockIdx.x * ntile / gridDim.x);
+  const int t_end = (int)((long long)(blockIdx.x + 1) * ntile / gridDim.x);
+  const int r_begin = t_begin * R;
+  const int nrows = min(a.N, t_end * R) - r_begin;
+  const int nblk = t_end - t_begin;
   const bool has_z = (FMT != FMT_MXFP4) && a.zeros != nullptr;
 
   // chunk bookkeeping; a chunk past the row end is clamped onto the last real
@@ -89,22 +94,27 @@ __global__ void __launch_bounds__(ROWS_MAX_WARPS * 32) gemv_rows_kernel(const Ge
   float sc[2][R][CH];
   uint32_t zz[2][R][CH];
   (void)zz;
-  auto load = [&](int b, int buf) {
+  auto load_row = [&](int b, int j, int buf) {
+    const int rr = b * R + j;
 #pragma unroll
-    for (int j = 0; j < R; ++j) {
-      const int rr = b * R + j;
-      if (rr < nrows) {
-#pragma unroll
-        for (int i = 0; i < CH; ++i) {
-          w[buf][j][i] = ldg_stream(qbase + (size_t)rr * RB + (ch_c[i] << 4), pol);
-          if (FMT == FMT_MXFP4) {
-            sc[buf][j][i] = e8m0_half_scale(__ldg(ebase + (size_t)rr * NB32 + ch_c[i]));
-          } else {
-            sc[buf][j][i] = __ldg(sbase + (size_t)rr * G + (ch_c[i] >> 2));
-            zz[buf][j][i] = has_z ? (uint32_t)__ldg(zbase + (size_t)rr * G + (ch_c[i] >> 2)) : 8u;
-          }
-        }
+    for (int i = 0; i < CH; ++i) {
+      w[buf][j][i] = ldg_stream(qbase + (size_t)rr * RB + (ch_c[i] << 4), pol);
+      if (FMT == FMT_MXFP4) {
+        sc[buf][j][i] = e8m0_half_scale(__ldg(ebase + (size_t)rr * NB32 + ch_c[i]));
+      } else {
+        sc[buf][j][i] = __ldg(sbase + (size_t)rr * G + (ch_c[i] >> 2));
+        zz[buf][j][i] = has_z ? (uint32_t)__ldg(zbase + (size_t)rr * G + (ch_c[i] >> 2)) : 8u;
       }
+    }
+  };
+  auto load = [&](int b, int buf) {
+    if (b * R + R <= nrows) {
+#pragma unroll
+      for (int j = 0; j < R; ++j) load_row(b, j, buf);
+    } else {
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (b * R + j < nrows) load_row(b, j, buf);
     }
   };
 
