@@ -199,6 +199,36 @@ int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw,
                              uint32_t *epoch, int rank, int world, const lbc_params *p,
                              void *stream);
 
+/* ---- decoder-layer operators around the GEMMs (the model-side callers of
+ * the reference, src/lowbit/model.py:380-433, on the GPU). fp32 activations,
+ * row-major; `pos` is a DEVICE int32 holding the number of tokens already in
+ * the KV cache, read by the kernels (CUDA graphs of a decode step replay at
+ * every position). B sequences of T tokens each share one position; token
+ * row i is (sequence i / T, step i % T). KV caches of one layer are
+ * [B, KV, S_max, D]. All return 0 or a negative LBC_ERR_*. */
+
+/* out = x' / sqrt(mean(x'^2) + eps) * w per row of H, x' = x + residual when
+ * residual is non-NULL (then also stored to x_out, which may alias x)
+ * (src/lowbit/model.py:188-190 with the residual adds of :413 and :421). */
+int lbc_rmsnorm(const float *x, const float *residual, float *x_out, const float *w,
+                float *out, int T, int H, float eps, void *stream);
+/* qkv [B*T, (H + 2*KV)*D] (+ bias [(H + 2*KV)*D] when non-NULL): rotate-half
+ * RoPE at position pos + t (cos/sin tables [positions, D/2]) on the q and k
+ * heads; q to q_out [B*T, H, D], k and v into the caches at pos + t
+ * (src/lowbit/model.py:199-208, :343-345, :403-406). */
+int lbc_qkv_rope(const float *qkv, const float *bias, const float *cos_t, const float *sin_t,
+                 const int32_t *pos, float *q_out, float *k_cache, float *v_cache, int B, int T,
+                 int H, int KV, int D, int S_max, void *stream);
+/* causal grouped-query attention: query (i, h) attends to keys 0..pos + i % T
+ * of KV head h / (H / KV); out [B*T, H*D] (src/lowbit/model.py:336-361).
+ * D is 32, 64 or 128. */
+int lbc_attention(const float *q, const float *k_cache, const float *v_cache, const int32_t *pos,
+                  float *out, int B, int T, int H, int KV, int D, int S_max, void *stream);
+/* out [T, I] = silu(gu[:, :I]) * gu[:, I:] (src/lowbit/model.py:211-212, :417). */
+int lbc_silu_mul(const float *gu, float *out, int T, int I, void *stream);
+/* *pos += n on the device, in stream order (end of a captured decode step). */
+int lbc_advance_pos(int32_t *pos, int n, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
