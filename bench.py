@@ -18,6 +18,18 @@ Our arm ("ours"):
     every step, synchronised per step.
 Reference arm: lowbit's own CPU kernels (compiled from the reference's sources
 into oracle/_ref) on all host cores, same config, same metric.
+
+    python bench.py --workload model [--steps K] [--warmup W]
+
+Model workload: the Qwen2-0.5B-shaped decoder (24
+layers, hidden 896, 14/2 heads, SwiGLU 4864, vocabulary 151936, tied
+embeddings), random weights (random_weights(seed 0, scale 0.02): N(0, 0.02)
+linears, the generator's x20 embedding and 1 + r norms), every linear int4
+g128 asym; a 128-token prompt then 128 greedy tokens at batch 1 and 16.
+Reports decode and prefill tokens/s and max |delta logit| against the
+reference's computation on the host (its C kernels for every linear, the
+numpy glue restated in oracle/model_ref.py), whose decode is also timed as
+the CPU baseline.
 """
 from __future__ import annotations
 
@@ -410,6 +422,103 @@ def _ncu_traffic(workload: str):
         return None
 
 
+# ---------------------------------------------------------------- model workload
+MODEL_METRIC = "Qwen2-0.5B-shape greedy decode tokens/s (w4a16 int4-g128 asym, batch 1)"
+
+
+def run_model(args) -> dict:
+    import torch
+    from lowbit_b200 import model as PM
+    from oracle import model_ref as O
+    from oracle import ref_lib
+
+    cfg = PM.qwen2_0_5b_config()
+    t_build = time.perf_counter()
+    W = PM.random_weights(cfg, seed=0, scale=0.02)
+    m = PM.Model(cfg, W, backend="w4a16", asym=True)
+    t_build = time.perf_counter() - t_build
+    V, P, NEW = cfg.vocab_size, 128, 128
+    prompt = np.random.default_rng(0).integers(0, V, P)
+    prompts16 = np.random.default_rng(1).integers(0, V, (16, P))
+    c1, c16 = m.new_cache(P + NEW), m.new_cache(P + NEW, batch=16)
+    for _ in range(args.warmup):  # builds plans, workspaces and the decode graphs
+        c1.reset()
+        m.generate(prompt, 4, cache=c1)
+        c16.reset()
+        m.generate_batch(prompts16, 4, cache=c16)
+    clk = ClockSampler(torch.cuda.current_device())
+    clk.start()
+    runs1, runs16, toks = [], [], None
+    for _ in range(args.steps):
+        c1.reset()
+        t = {}
+        toks = m.generate(prompt, NEW, cache=c1, timings=t)
+        runs1.append(t)
+        c16.reset()
+        t = {}
+        m.generate_batch(prompts16, NEW, cache=c16, timings=t)
+        runs16.append(t)
+    clocks = clk.stop()
+
+    def med(runs, key):
+        return statistics.median(r[key] for r in runs)
+
+    dec1 = (NEW - 1) / med(runs1, "decode_s")
+    dec16 = 16 * (NEW - 1) / med(runs16, "decode_s")
+    line = {"metric": MODEL_METRIC, "value": round(dec1, 1), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / dec1, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: random_weights(seed 0, scale 0.02), prompt default_rng(0).integers(0, 151936, 128)",
+            "config": {"workload": "Qwen2-0.5B-shaped decoder, w4a16 asym linears, prompt 128, 128 greedy tokens "
+                                   "(BASELINE configs[4])", "layers": cfg.num_layers, "hidden": cfg.hidden_size,
+                       "vocab": V, "prompt": P, "new_tokens": NEW,
+                       "timing": "decode: 127 CUDA-graph replays of a whole decode step (host clock around "
+                                 "synchronised loops); a step = one token for every sequence of the batch"},
+            "prefill_tok_s": round(P / med(runs1, "prefill_s"), 1),
+            "batch16": {"decode_tok_s": round(dec16, 1), "prefill_tok_s": round(16 * P / med(runs16, "prefill_s"), 1),
+                        "ms_per_step": round(1e3 * med(runs16, "decode_s") / (NEW - 1), 4)},
+            "build_s": round(t_build, 1), "clocks": clocks}
+    # parity and CPU baseline: the reference's computation on the host (its C
+    # kernels for every linear), prefill then 3 teacher-forced decode steps
+    if ref_lib.available():
+        threads = os.cpu_count() or 1
+        ocfg = O.Cfg(**{k: getattr(cfg, k) for k in O.Cfg.__dataclass_fields__})
+        lin = {}
+        for key, (w, b) in O.concat_weights(ocfg, W).items():
+            lin[key] = O.lin_ref_c("w4a16", (m.lm_head if key == "lm_head" else
+                                             getattr(m.layers[key[0]], key[1])).wq, b, threads)
+        ref = O.Model(ocfg, W, lin)
+        oc = O.new_cache(ocfg, P + 8)
+        c1.reset()
+        feed = [int(t) for t in toks[:3]]
+        d_abs, scale = 0.0, 0.0
+        t0 = time.perf_counter()
+        lo = ref.forward(prompt, oc)
+        t_pre = time.perf_counter() - t0
+        lg = m.forward(prompt, c1)
+        d_abs, scale = max(d_abs, float(np.abs(lg - lo).max())), max(scale, float(np.abs(lo).max()))
+        td = []
+        for tk in feed:
+            t0 = time.perf_counter()
+            lo = ref.forward([tk], oc)
+            td.append(time.perf_counter() - t0)
+            lg = m.forward([tk], c1)
+            d_abs, scale = max(d_abs, float(np.abs(lg - lo).max())), max(scale, float(np.abs(lo).max()))
+        cpu_dec = 1.0 / statistics.median(td)
+        line["max_abs_dlogit"] = round(d_abs, 6)
+        line["rel_dlogit"] = float(f"{d_abs / scale:.3e}")
+        line["parity_note"] = ("logits of the 128-token prefill (bf16 prefill GEMMs, 4e-3 contract) and 3 decode "
+                               "steps (exact fp32 decode GEMMs) vs the reference's C kernels + numpy glue")
+        line["cpu_baseline"] = {"value": round(cpu_dec, 2), "unit": "tok/s", "cores": threads, "kind": "reference",
+                                "sample": f"3 decode steps after a 128-token prefill ({t_pre:.1f} s): lowbit "
+                                          "lb_gemm_w4a16 for every linear (oracle/_ref) with the numpy glue, "
+                                          "default tiles"}
+    else:
+        line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
+                                "sample": "unavailable: oracle/_ref/liblowbit_ref.so not built"}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -418,9 +527,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["decode", "model"], default="decode")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "model":
+        if args.steps > 50:
+            args.steps = 3  # a step is a whole 128-token generation here
+        print(json.dumps(run_model(args)), flush=True)
+        return
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:
             return

@@ -199,6 +199,18 @@ int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw,
                              uint32_t *epoch, int rank, int world, const lbc_params *p,
                              void *stream);
 
+/* ---- on-device weight quantizers: bit-identical to the reference's numpy
+ * quantizers (src/lowbit/formats.py:90-142 and :175-212), writing the packed
+ * layouts above from a row-major fp32 W [N, K] in device memory (Kp = K
+ * rounded up to 128, resp. 32; padding gets the code that decodes to 0).
+ * mode: 0 absmax (symmetric), 1 asym (zeros required), 2 signed-max. */
+#define LBC_QUANT_ABSMAX 0
+#define LBC_QUANT_ASYM 1
+#define LBC_QUANT_SIGNED_MAX 2
+int lbc_quantize_int4(const float *w, int N, int K, int mode, uint8_t *qw, float *scales,
+                      uint8_t *zeros, void *stream);
+int lbc_quantize_mxfp4(const float *w, int N, int K, uint8_t *qw, uint8_t *e8m0, void *stream);
+
 /* ---- decoder-layer operators around the GEMMs (the model-side callers of
  * the reference, src/lowbit/model.py:380-433, on the GPU). fp32 activations,
  * row-major; `pos` is a DEVICE int32 holding the number of tokens already in
@@ -221,9 +233,31 @@ int lbc_qkv_rope(const float *qkv, const float *bias, const float *cos_t, const 
                  int H, int KV, int D, int S_max, void *stream);
 /* causal grouped-query attention: query (i, h) attends to keys 0..pos + i % T
  * of KV head h / (H / KV); out [B*T, H*D] (src/lowbit/model.py:336-361).
- * D is 32, 64 or 128. */
+ * D is 32, 64 or 128; at most 16 query heads per KV head; the scores of one
+ * token's head group, G * S_max fp32, must fit in shared memory (227 KB). */
 int lbc_attention(const float *q, const float *k_cache, const float *v_cache, const int32_t *pos,
                   float *out, int B, int T, int H, int KV, int D, int S_max, void *stream);
+/* W4A16 decode GEMMs with the operator before them fused into the kernel's
+ * activation load (M <= 2 and default params only; otherwise LBC_ERR_PARAMS
+ * and nothing runs, so the caller uses the separate kernels):
+ *   _rmsnorm: y = lbc_rmsnorm(x, residual, x_out, norm_w, eps) . W^T, with
+ *             x + residual stored to x_out (a buffer distinct from x and
+ *             residual) when residual is non-NULL; K = Kp.
+ *   _glu:     y = (silu(gu[:, :Kp]) * gu[:, Kp:]) . W^T, gu rows of 2*Kp
+ *             (lbc_silu_mul then the GEMM).
+ * Results equal the two-kernel path up to the order of the norm's sum of
+ * squares. Returns LBC_PATH_SIMT or a negative LBC_ERR_*. */
+int lbc_gemm_w4a16_rmsnorm(const float *x, const float *residual, float *x_out, const float *norm_w,
+                           float eps, int M, int Kp, const uint8_t *qw, const float *scales,
+                           const uint8_t *zeros, int N, float *y, const lbc_params *p, void *stream);
+int lbc_gemm_w4a16_glu(const float *gu, int M, int Kp, const uint8_t *qw, const float *scales,
+                       const uint8_t *zeros, int N, float *y, const lbc_params *p, void *stream);
+/* One-token steps (T == 1): lbc_qkv_rope and lbc_attention in one launch --
+ * each (sequence, KV head) CTA ropes its query heads and appends its k and v
+ * at pos before attending. qkv [B, (H + 2*KV)*D], out [B, H*D]. */
+int lbc_rope_attention(const float *qkv, const float *bias, const float *cos_t, const float *sin_t,
+                       const int32_t *pos, float *k_cache, float *v_cache, float *out, int B, int H,
+                       int KV, int D, int S_max, void *stream);
 /* out [T, I] = silu(gu[:, :I]) * gu[:, I:] (src/lowbit/model.py:211-212, :417). */
 int lbc_silu_mul(const float *gu, float *out, int T, int I, void *stream);
 /* *pos += n on the device, in stream order (end of a captured decode step). */

@@ -263,7 +263,9 @@ int plan_rows(int fmt, int M, int N, int Kp, const lbc_params *p, RowsPlan &P) {
   if (!lbc::rows_combo(P.mt, P.ch, P.r)) return fail(LBC_ERR_PARAMS, "decode tile not compiled");
   const int occ = rows_occupancy_cached(fmt, P.mt, P.ch, P.r, P.threads);
   if (occ <= 0) return fail(LBC_ERR_PARAMS, "decode kernel cannot be resident on an SM");
-  P.cps = std::min((p && p->nb > 0) ? p->nb : 4, occ);
+  // about 16 resident warps per SM by default: small-K rows (one-warp teams)
+  // need many CTAs per SM to keep enough loads in flight
+  P.cps = std::min((p && p->nb > 0) ? p->nb : std::max(4, 16 / nw), occ);
   // the kernel hands out whole blocks of r rows
   P.grid = std::max(1, std::min(ceil_div(N, P.r), di.sms * P.cps));
   return 0;
@@ -439,6 +441,46 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
   a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
   a.M = M; a.N = N; a.Kp = Kp;
   return run_gemv(lbc::FMT_W4A16, a, p, static_cast<cudaStream_t>(stream));
+}
+
+// W4A16 decode with a fused activation prologue (rows kernel only: M <= 2,
+// default tiling); LBC_ERR_PARAMS tells the caller to run the two-kernel path
+static int run_fused_w4a16(lbc::GemvArgs a, int xm, const lbc_params *p, cudaStream_t st) {
+  if (!rows_eligible(lbc::FMT_W4A16, a.M, a.Kp, p) || (p && (p->isa == LBC_PATH_TCGEN05 || p->nb > 0)))
+    return fail(LBC_ERR_PARAMS, "fused decode prologue: M <= 2 with default tiling only");
+  RowsPlan P;
+  if (int rc = plan_rows(lbc::FMT_W4A16, a.M, a.N, a.Kp, p, P)) return rc;
+  a.status = dev_info().status;
+  cudaError_t e = lbc::rows_fused_launch(a, xm, P.mt, P.ch, P.r, dim3(P.grid, 1, 1), P.threads, st);
+  if (e != cudaSuccess) return fail_cuda("fused decode gemv launch", e);
+  return LBC_PATH_SIMT;
+}
+
+int lbc_gemm_w4a16_rmsnorm(const float *x, const float *residual, float *x_out, const float *norm_w, float eps,
+                           int M, int Kp, const uint8_t *qw, const float *scales, const uint8_t *zeros, int N,
+                           float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (!x || !norm_w || !qw || !scales || !y || !al16(x) || !al16(qw) || !al16(norm_w) ||
+      (residual && (!al16(residual) || !x_out)) || (x_out && (x_out == x || x_out == residual)))
+    return fail(LBC_ERR_SHAPE, "NULL, misaligned or aliasing pointer (x_out must be a separate buffer)");
+  if (int rc = device_gate()) return rc;
+  lbc::GemvArgs a{};
+  a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+  a.M = M; a.N = N; a.Kp = Kp;
+  a.xres = residual; a.xout = residual ? x_out : nullptr; a.lnw = norm_w; a.eps = eps;
+  return run_fused_w4a16(a, lbc::XM_RMSNORM, p, static_cast<cudaStream_t>(stream));
+}
+
+int lbc_gemm_w4a16_glu(const float *gu, int M, int Kp, const uint8_t *qw, const float *scales,
+                       const uint8_t *zeros, int N, float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (!gu || !qw || !scales || !y || !al16(gu) || !al16(qw))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer");
+  if (int rc = device_gate()) return rc;
+  lbc::GemvArgs a{};
+  a.x = gu; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+  a.M = M; a.N = N; a.Kp = Kp;
+  return run_fused_w4a16(a, lbc::XM_GLU, p, static_cast<cudaStream_t>(stream));
 }
 
 int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8_t *e8m0, int N,

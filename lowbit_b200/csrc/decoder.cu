@@ -5,7 +5,8 @@
 //                (src/lowbit/model.py:188-190 and the residual adds at :413, :421)
 //   qkv_rope     bias add (the linear's y += b, :119-124), rotate-half RoPE on q and
 //                k (:199-208), k and v appended to the KV cache (:343-345)
-//   attention    causal grouped-query softmax attention over the cache (:336-361)
+//   attention    causal grouped-query softmax attention over the cache (:336-361),
+//                one CTA per (token, KV head) sharing the K/V loads of its query heads
 //   silu_mul     silu(gate) * up (:211-212, :417)
 //
 // Every operator reads the position from device memory, so one captured CUDA
@@ -26,7 +27,7 @@ namespace lbc {
 namespace {
 
 constexpr int NORM_THREADS = 256;
-constexpr int ATT_THREADS = 128;
+constexpr int ATT_THREADS = 512;
 
 __device__ __forceinline__ float block_sum(float v, float *red) {
 #pragma unroll
@@ -37,18 +38,6 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
   __syncthreads();
   float t = 0.f;
   for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
-}
-
-__device__ __forceinline__ float block_max(float v, float *red) {
-#pragma unroll
-  for (int s = 16; s >= 1; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = red[0];
-  for (int i = 1; i < nw; ++i) t = fmaxf(t, red[i]);
   return t;
 }
 
@@ -114,60 +103,145 @@ __global__ void qkv_rope_kernel(const float *qkv, const float *bias, const float
   }
 }
 
-// one CTA per (token, query head): scores over keys 0..pos+t in shared memory
-template <int DPL>  // head elements per lane (D = 32 * DPL)
-__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, const float *k_cache,
-                                                                const float *v_cache, const int32_t *pos_p,
-                                                                float *out, int T, int H, int KV, int S_max,
-                                                                float scale) {
-  extern __shared__ float sc[];  // [S_max] scores, then [ATT_THREADS] partial outputs
-  __shared__ float red[ATT_THREADS / 32];
-  constexpr int D = 32 * DPL;
-  const int i = blockIdx.x, h = blockIdx.y, b = i / T, t = i % T;
-  const int L = *pos_p + t + 1;
-  const int kvh = h / (H / KV);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const float *qv = q + ((size_t)i * H + h) * D;
-  float qr[DPL];
+// One CTA per (token, KV head): the G = H / KV query heads that share the KV
+// head share its K and V loads (G <= ATT_MAX_G). Scores: thread t takes keys
+// t, t + 512, ... and computes all G dot products from its own loads (q in
+// shared memory, read as broadcasts). Softmax: warp w normalises heads w,
+// w + 16, ... Output: thread (key group, element d) accumulates all G heads
+// over keys j = group (mod groups), one load of v[j][d] serving every head,
+// then the groups' partial sums are added in a fixed order.
+//
+// FUSE_ROPE (single-token steps, T == 1): the CTA first does lbc_qkv_rope's
+// work for its heads -- bias, RoPE, q to shared memory, k and v of its KV head
+// appended to the cache at pos -- so a decode step needs no separate launch.
+// (With T > 1 other tokens' keys come from other CTAs, so prefill runs the
+// two kernels separately.)
+constexpr int ATT_MAX_G = 16;
+
+template <int D, bool FUSE_ROPE>
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, const float *bias,
+                                                                const float *cos_t, const float *sin_t,
+                                                                float *k_cache, float *v_cache,
+                                                                const int32_t *pos_p, float *out, int T, int H,
+                                                                int KV, int S_max, float scale) {
+  extern __shared__ float4 smem4[];
+  const int G = H / KV;
+  constexpr int NG = ATT_THREADS / D;  // key groups in the output phase
+  float *qs = reinterpret_cast<float *>(smem4);  // [G][D]
+  float *part = qs + G * D;                       // [NG][G][D] output partials
+  float *sc = part + NG * G * D;                  // [G][L] scores
+  const int i = blockIdx.x, kvh = blockIdx.y, b = i / T, t = i % T;
+  const int p0 = *pos_p;
+  const int L = p0 + t + 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NWARP = ATT_THREADS / 32;
+  float *kb = k_cache + ((size_t)b * KV + kvh) * S_max * D;
+  float *vb = v_cache + ((size_t)b * KV + kvh) * S_max * D;
+  if (FUSE_ROPE) {
+    // q rows of this group's heads, then k and v of the KV head, as lbc_qkv_rope
+    constexpr int half = D / 2;
+    const int W = (H + 2 * KV) * D;
+    const float *row = q + (size_t)i * W;
+    const float *cs = cos_t + (size_t)(p0 + t) * half, *sn = sin_t + (size_t)(p0 + t) * half;
+    for (int e = tid; e < (G + 1) * half; e += ATT_THREADS) {
+      const int hh = e / half, d = e % half;
+      const int head = hh < G ? kvh * G + hh : H + kvh;
+      const int c1 = head * D + d, c2 = c1 + half;
+      float x1 = row[c1], x2 = row[c2];
+      if (bias) {
+        x1 = __fadd_rn(x1, bias[c1]);
+        x2 = __fadd_rn(x2, bias[c2]);
+      }
+      const float c = cs[d], sv = sn[d];
+      const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sv));
+      const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sv));
+      if (hh < G) {
+        qs[hh * D + d] = o1;
+        qs[hh * D + d + half] = o2;
+      } else {
+        kb[(size_t)(p0 + t) * D + d] = o1;
+        kb[(size_t)(p0 + t) * D + d + half] = o2;
+      }
+    }
+    for (int d = tid; d < D; d += ATT_THREADS) {
+      const int c = (H + KV + kvh) * D + d;
+      float v = row[c];
+      if (bias) v = __fadd_rn(v, bias[c]);
+      vb[(size_t)(p0 + t) * D + d] = v;
+    }
+  } else {
+    const float *qb = q + ((size_t)i * H + (size_t)kvh * G) * D;
+    for (int e = tid; e < G * D; e += ATT_THREADS) qs[e] = qb[e];
+  }
+  __syncthreads();  // also orders this CTA's cache writes before its reads below
+  for (int j = tid; j < L; j += ATT_THREADS) {
+    // the key row in slices of 32 elements; each head's dot product runs
+    // over d = 0..D-1 in order
+    const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)j * D);
+    float s[ATT_MAX_G];
 #pragma unroll
-  for (int u = 0; u < DPL; ++u) qr[u] = qv[lane + 32 * u];
-  const float *kb = k_cache + ((size_t)b * KV + kvh) * S_max * D;
-  const float *vb = v_cache + ((size_t)b * KV + kvh) * S_max * D;
-  for (int j = warp; j < L; j += nw) {
-    const float *kr = kb + (size_t)j * D;
-    float s = 0.f;
+    for (int h = 0; h < ATT_MAX_G; ++h) s[h] = 0.f;
 #pragma unroll
-    for (int u = 0; u < DPL; ++u) s = __fmaf_rn(qr[u], kr[lane + 32 * u], s);
+    for (int u0 = 0; u0 < D / 4; u0 += 8) {
+      float4 kv[8];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) sc[j] = __fmul_rn(s, scale);
+      for (int u = 0; u < 8; ++u) kv[u] = kr[u0 + u];
+#pragma unroll
+      for (int h = 0; h < ATT_MAX_G; ++h) {
+        if (h < G) {
+          const float4 *qh = reinterpret_cast<const float4 *>(qs + h * D) + u0;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float4 a = qh[u];
+            s[h] = __fmaf_rn(a.x, kv[u].x, s[h]);
+            s[h] = __fmaf_rn(a.y, kv[u].y, s[h]);
+            s[h] = __fmaf_rn(a.z, kv[u].z, s[h]);
+            s[h] = __fmaf_rn(a.w, kv[u].w, s[h]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_G; ++h)
+      if (h < G) sc[h * L + j] = __fmul_rn(s[h], scale);
   }
   __syncthreads();
-  float mx = -INFINITY;
-  for (int j = threadIdx.x; j < L; j += blockDim.x) mx = fmaxf(mx, sc[j]);
-  mx = block_max(mx, red);
-  float sum = 0.f;
-  for (int j = threadIdx.x; j < L; j += blockDim.x) {
-    const float e = expf(__fsub_rn(sc[j], mx));
-    sc[j] = e;
-    sum = __fadd_rn(sum, e);
+  for (int h = warp; h < G; h += NWARP) {
+    float *row = sc + h * L;
+    float mx = -INFINITY;
+    for (int j = lane; j < L; j += 32) mx = fmaxf(mx, row[j]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < L; j += 32) {
+      const float e = expf(__fsub_rn(row[j], mx));
+      row[j] = e;
+      sum = __fadd_rn(sum, e);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int j = lane; j < L; j += 32) row[j] = __fdiv_rn(row[j], sum);
   }
-  sum = block_sum(sum, red);
-  for (int j = threadIdx.x; j < L; j += blockDim.x) sc[j] = __fdiv_rn(sc[j], sum);
   __syncthreads();
-  // out[d] = sum_j p_j v_j[d]: thread (group g, element d) takes keys j = g mod groups
-  const int groups = blockDim.x / D;
-  const int d = threadIdx.x % D, g = threadIdx.x / D;
-  float acc = 0.f;
-  if (g < groups)
-    for (int j = g; j < L; j += groups) acc = __fmaf_rn(sc[j], vb[(size_t)j * D + d], acc);
-  float *part = sc + S_max;
-  part[threadIdx.x] = acc;
+  const int d = tid % D, kg = tid / D;
+  float acc[ATT_MAX_G];
+#pragma unroll
+  for (int h = 0; h < ATT_MAX_G; ++h) acc[h] = 0.f;
+#pragma unroll 8
+  for (int j = kg; j < L; j += NG) {
+    const float v = vb[(size_t)j * D + d];
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_G; ++h)
+      if (h < G) acc[h] = __fmaf_rn(sc[h * L + j], v, acc[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < ATT_MAX_G; ++h)
+    if (h < G) part[(kg * G + h) * D + d] = acc[h];
   __syncthreads();
-  if (threadIdx.x < D) {
+  for (int e = tid; e < G * D; e += ATT_THREADS) {
     float o = 0.f;
-    for (int gg = 0; gg < groups; ++gg) o = __fadd_rn(o, part[gg * D + threadIdx.x]);
-    out[((size_t)i * H + h) * D + threadIdx.x] = o;
+    for (int g = 0; g < NG; ++g) o = __fadd_rn(o, part[g * G * D + e]);
+    out[((size_t)i * H + (size_t)kvh * G) * D + e] = o;
   }
 }
 
@@ -224,27 +298,56 @@ int lbc_qkv_rope(const float *qkv, const float *bias, const float *cos_t, const 
   return launch_status("qkv_rope");
 }
 
-int lbc_attention(const float *q, const float *k_cache, const float *v_cache, const int32_t *pos, float *out,
-                  int B, int T, int H, int KV, int D, int S_max, void *stream) {
+}  // extern "C"
+
+namespace lbc {
+namespace {
+int attention_launch(const float *q, const float *bias, const float *cos_t, const float *sin_t, float *k_cache,
+                     float *v_cache, const int32_t *pos, float *out, int B, int T, int H, int KV, int D, int S_max,
+                     bool fuse, cudaStream_t st) {
   if (B <= 0 || T <= 0 || H <= 0 || KV <= 0 || H % KV || S_max <= 0) return shape_error("attention: bad shape");
   if (D != 32 && D != 64 && D != 128) return shape_error("attention: head_dim must be 32, 64 or 128");
-  const size_t smem = ((size_t)S_max + ATT_THREADS) * sizeof(float);
+  const int G = H / KV;
+  if (G > ATT_MAX_G) return shape_error("attention: more than 16 query heads per KV head");
+  const size_t smem = ((size_t)G * D * (1 + ATT_THREADS / D) + (size_t)G * S_max) * sizeof(float);
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  if (smem + 64 > (size_t)optin) return shape_error("attention: KV cache longer than shared memory allows");
-  const dim3 grid(B * T, H);
+  if (smem > (size_t)optin) return shape_error("attention: KV cache longer than shared memory allows");
+  const dim3 grid(B * T, KV);
   const float scale = (float)(1.0 / std::sqrt((double)D));  // np.float32(1.0 / np.sqrt(D))
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define LBC_ATT(DPL)                                                                                     \
-  {                                                                                                      \
-    auto k = attention_kernel<DPL>;                                                                      \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    k<<<grid, ATT_THREADS, smem, st>>>(q, k_cache, v_cache, pos, out, T, H, KV, S_max, scale);           \
+#define LBC_ATT(DD, F)                                                                                     \
+  {                                                                                                        \
+    auto k = attention_kernel<DD, F>;                                                                      \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);   \
+    k<<<grid, ATT_THREADS, smem, st>>>(q, bias, cos_t, sin_t, k_cache, v_cache, pos, out, T, H, KV, S_max,   \
+                                       scale);                                                             \
   }
-  if (D == 32) LBC_ATT(1) else if (D == 64) LBC_ATT(2) else LBC_ATT(4)
+  if (fuse) {
+    if (D == 32) LBC_ATT(32, true) else if (D == 64) LBC_ATT(64, true) else LBC_ATT(128, true)
+  } else {
+    if (D == 32) LBC_ATT(32, false) else if (D == 64) LBC_ATT(64, false) else LBC_ATT(128, false)
+  }
 #undef LBC_ATT
   return launch_status("attention");
+}
+}  // namespace
+}  // namespace lbc
+
+extern "C" {
+
+int lbc_attention(const float *q, const float *k_cache, const float *v_cache, const int32_t *pos, float *out,
+                  int B, int T, int H, int KV, int D, int S_max, void *stream) {
+  return attention_launch(q, nullptr, nullptr, nullptr, const_cast<float *>(k_cache), const_cast<float *>(v_cache),
+                          pos, out, B, T, H, KV, D, S_max, false, static_cast<cudaStream_t>(stream));
+}
+
+int lbc_rope_attention(const float *qkv, const float *bias, const float *cos_t, const float *sin_t,
+                       const int32_t *pos, float *k_cache, float *v_cache, float *out, int B, int H, int KV, int D,
+                       int S_max, void *stream) {
+  if (D % 2) return shape_error("rope_attention: odd head_dim");
+  return attention_launch(qkv, bias, cos_t, sin_t, k_cache, v_cache, pos, out, B, 1, H, KV, D, S_max, true,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int lbc_silu_mul(const float *gu, float *out, int T, int I, void *stream) {

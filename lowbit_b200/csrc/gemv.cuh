@@ -63,7 +63,17 @@ struct GemvArgs {
   uint32_t *counter;            // this rank's CTA completion counter
   uint32_t *epoch;              // this rank's call counter (the flags carry it)
   int rank, world, row0, ld_y;  // this rank's first global row, Y row stride
+  // fused activation prologue of the decode kernel (W4A16), else unused:
+  const float *xres;  // [M, Kp] residual added to x before the norm, or nullptr
+  float *xout;        // [M, Kp] x + xres, stored by the CTAs of column 0 (never aliases x)
+  const float *lnw;   // [Kp] RMSNorm weight
+  float eps;          // RMSNorm epsilon
 };
+
+// activation prologues of the decode kernel
+constexpr int XM_PLAIN = 0;    // x as given
+constexpr int XM_RMSNORM = 1;  // (x + xres) / sqrt(mean((x + xres)^2) + eps) * lnw
+constexpr int XM_GLU = 2;      // silu(x[:, :Kp]) * x[:, Kp:] (x rows of 2 * Kp)
 
 // Per-stage metadata region (scales + zero points, or E8M0 exponents) when it
 // is staged by TMA: bytes per row of each part, rounded regions per stage.

@@ -31,6 +31,24 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t pol) {
   return v;
 }
 
+__device__ __forceinline__ float4 zero4() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+__device__ __forceinline__ float sumsq4(float4 v, float s) {
+  s = __fmaf_rn(v.x, v.x, s);
+  s = __fmaf_rn(v.y, v.y, s);
+  s = __fmaf_rn(v.z, v.z, s);
+  return __fmaf_rn(v.w, v.w, s);
+}
+// silu(g) * u, rounded as the standalone SiLU-multiply kernel rounds it
+__device__ __forceinline__ float glu1(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+__device__ __forceinline__ float4 glu4(float4 g, float4 u) {
+  return make_float4(glu1(g.x, u.x), glu1(g.y, u.y), glu1(g.z, u.z), glu1(g.w, u.w));
+}
+
 __device__ __forceinline__ void st_relaxed_sys_u32(uint32_t *p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -56,8 +74,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
 // counter. When the kernel
 // completes, Y is whole on this GPU. No epoch is baked into the launch, so a
 // CUDA graph of these calls replays correctly.
-template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false>
+template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false, int XM = XM_PLAIN>
 __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
+  static_assert(XM == XM_PLAIN || FMT == FMT_W4A16, "fused prologues are W4A16 only");
   constexpr int V = R * MT;
   static_assert(V <= 32 && (V & (V - 1)) == 0, "R*MT must be a power of two <= 32");
   static_assert(NW >= 1 && NW <= ROWS_MAX_WARPS, "1..ROWS_MAX_WARPS warps per row team");
@@ -124,6 +143,14 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   pdl_launch_dependents();
   pdl_wait_prior_grid();
 
+  // RMSNorm prologue: the team's threads hold the whole row of x between them
+  // (CH * NT chunks cover Kp), so the sum of squares of x + residual comes
+  // from the registers the loads below fill; the factor is applied after a
+  // team-wide reduction
+  float ss[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) ss[t] = 0.f;
+  (void)ss;
   uint64_t xr[CH][MT][16];
   uint32_t xl[CH][MT][4], xh[CH][MT][4];
   int xsum[CH][MT];
@@ -158,19 +185,71 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
         // the reference applies it (src/lowbit/csrc/kern_scalar.c:49-59)
         xsum[i][t] = (ok && (c & 3) == 0) ? __ldg(a.asum + (size_t)m * G + (c >> 2)) : 0;
       } else {
-        const float4 *pl = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + lo);
-        const float4 *ph = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + hi);
+        const size_t xrow = (size_t)m * a.Kp * (XM == XM_GLU ? 2 : 1);
+        const float4 *pl = reinterpret_cast<const float4 *>(a.x + xrow + lo);
+        const float4 *ph = reinterpret_cast<const float4 *>(a.x + xrow + hi);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f), h4 = l4;
           if (ok) {
             l4 = __ldg(pl + q);
             h4 = __ldg(ph + q);
+            if (XM == XM_RMSNORM) {
+              if (a.xres) {
+                l4 = add4(l4, __ldg(reinterpret_cast<const float4 *>(a.xres + xrow + lo) + q));
+                h4 = add4(h4, __ldg(reinterpret_cast<const float4 *>(a.xres + xrow + hi) + q));
+                if (a.xout && blockIdx.x == 0) {
+                  reinterpret_cast<float4 *>(a.xout + xrow + lo)[q] = l4;
+                  reinterpret_cast<float4 *>(a.xout + xrow + hi)[q] = h4;
+                }
+              }
+              ss[t] = sumsq4(h4, sumsq4(l4, ss[t]));
+            } else if (XM == XM_GLU) {
+              l4 = glu4(l4, __ldg(pl + q + a.Kp / 4));
+              h4 = glu4(h4, __ldg(ph + q + a.Kp / 4));
+            }
           }
           xr[i][t][4 * q + 0] = pack2(__float_as_uint(l4.x), __float_as_uint(h4.x));
           xr[i][t][4 * q + 1] = pack2(__float_as_uint(l4.y), __float_as_uint(h4.y));
           xr[i][t][4 * q + 2] = pack2(__float_as_uint(l4.z), __float_as_uint(h4.z));
           xr[i][t][4 * q + 3] = pack2(__float_as_uint(l4.w), __float_as_uint(h4.w));
+        }
+      }
+    }
+  }
+  if (XM == XM_RMSNORM) {
+    __shared__ float nred[NW][MT];
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+      if (lane == 0) nred[warp][t] = ss[t];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      float tot = 0.f;
+      for (int ww = 0; ww < NW; ++ww) tot += nred[ww][t];
+      const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.Kp), a.eps)));
+#pragma unroll
+      for (int i = 0; i < CH; ++i) {
+        const int c = tid + i * NT;
+        const int lo = ((c >> 2) << 7) + ((c & 3) << 4), hi = lo + 64;
+        const bool ok = c < Cs;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float4 wl = zero4(), wh = zero4();
+          if (ok) {
+            wl = __ldg(reinterpret_cast<const float4 *>(a.lnw + lo) + q);
+            wh = __ldg(reinterpret_cast<const float4 *>(a.lnw + hi) + q);
+          }
+          const float wlv[4] = {wl.x, wl.y, wl.z, wl.w}, whv[4] = {wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint64_t v = xr[i][t][4 * q + e];
+            xr[i][t][4 * q + e] = pack2(__float_as_uint(__fmul_rn(__fmul_rn(lo_f(v), r), wlv[e])),
+                                        __float_as_uint(__fmul_rn(__fmul_rn(hi_f(v), r), whv[e])));
+          }
         }
       }
     }

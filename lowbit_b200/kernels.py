@@ -100,7 +100,13 @@ def lib() -> C.CDLL:
         "lbc_qkv_rope": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _int, _vp], _int),
         "lbc_attention": ([_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _int, _vp], _int),
         "lbc_silu_mul": ([_vp, _vp, _int, _int, _vp], _int),
+        "lbc_gemm_w4a16_rmsnorm": ([_vp, _vp, _vp, _vp, C.c_float, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp],
+                                   _int),
+        "lbc_gemm_w4a16_glu": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
+        "lbc_rope_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _vp], _int),
         "lbc_advance_pos": ([_vp, _int, _vp], _int),
+        "lbc_quantize_int4": ([_vp, _int, _int, _int, _vp, _vp, _vp, _vp], _int),
+        "lbc_quantize_mxfp4": ([_vp, _int, _int, _vp, _vp, _vp], _int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(so, name)
@@ -335,6 +341,45 @@ def w4a8_group_acc(a: Int8Acts, w: Int4Weights, isa=None):
                  None if d.zeros is None else d.zeros.data_ptr(), w.n, out.data_ptr(), -1, _stream()),
            "lbc_w4a8_group_acc")
     return out.cpu().numpy() if host else out
+
+
+# ---------------------------------------------------------------- on-device quantizers
+
+_QMODE = {("absmax", False): 0, ("absmax", True): 1, ("signed-max", False): 2}
+
+
+def quantize_int4_cuda(w, asym: bool = False, scale: str = "absmax") -> Int4Weights:
+    """formats.quantize_int4 on the GPU, bit for bit: W fp32 [N, K] (numpy or
+    torch) -> Int4Weights with CUDA tensors."""
+    from ._torch import to_cuda
+    torch = _torch()
+    if scale not in ("absmax", "signed-max"):
+        raise ValueError(f"scale must be 'absmax' or 'signed-max', not {scale!r}")
+    if asym and scale != "absmax":
+        raise ValueError("scale='signed-max' is a symmetric rule (asym=False)")
+    wt = to_cuda(w).to(torch.float32).contiguous()
+    n, k = (int(d) for d in wt.shape)
+    kp = -(-k // GROUP) * GROUP
+    qw = torch.empty((n, kp // 2), dtype=torch.uint8, device=wt.device)
+    sc = torch.empty((n, kp // GROUP), dtype=torch.float32, device=wt.device)
+    z = torch.empty((n, kp // GROUP), dtype=torch.uint8, device=wt.device) if asym else None
+    _check(_call("lbc_quantize_int4", wt.data_ptr(), n, k, _QMODE[(scale, bool(asym))], qw.data_ptr(),
+                 sc.data_ptr(), None if z is None else z.data_ptr(), _stream()), "lbc_quantize_int4")
+    return Int4Weights(qw, sc, z, k)
+
+
+def quantize_mxfp4_cuda(w) -> MXFP4Weights:
+    """formats.quantize_mxfp4 on the GPU, bit for bit."""
+    from ._torch import to_cuda
+    torch = _torch()
+    wt = to_cuda(w).to(torch.float32).contiguous()
+    n, k = (int(d) for d in wt.shape)
+    kp = -(-k // 32) * 32
+    qw = torch.empty((n, kp // 2), dtype=torch.uint8, device=wt.device)
+    e = torch.empty((n, kp // 32), dtype=torch.uint8, device=wt.device)
+    _check(_call("lbc_quantize_mxfp4", wt.data_ptr(), n, k, qw.data_ptr(), e.data_ptr(), _stream()),
+           "lbc_quantize_mxfp4")
+    return MXFP4Weights(qw, e, k)
 
 
 def describe_plan(kind: str, m: int, n: int, kp: int, params: Params | None = None, isa=None) -> dict:

@@ -14,6 +14,9 @@ fused in and the KV-cache append, lbc_attention, lbc_silu_mul). Positions
 live in device memory, so a whole decode step (embedding, 24 layers, head,
 argmax) is captured once as a CUDA graph and replayed for every token.
 Activations, norms, biases and the KV cache are fp32, as in the reference.
+Weights are quantized on the GPU (lbc_quantize_int4 / lbc_quantize_mxfp4,
+bit-identical to the numpy quantizers), so loading never round-trips W
+through the host quantizer.
 
 Beyond the reference: several sequences of equal length decode together
 (generate_batch): their rows share every GEMM, so the weights stream once
@@ -28,7 +31,7 @@ from pathlib import Path
 
 import numpy as np
 
-from .formats import quantize_int4, quantize_mxfp4
+from .kernels import quantize_int4_cuda, quantize_mxfp4_cuda
 
 BACKENDS = ("fp32", "w4a16", "w4a8", "mxfp4")
 
@@ -212,11 +215,16 @@ class _LowbitLinear(Linear):
     """A quantized linear: the library GEMM on device-resident packed weights."""
     fn = ""
 
-    def _setup(self, wq, params):
-        self.wq = wq
-        self.d = wq.cuda()
+    def _setup(self, d, params):
+        """d: the packed weights on the GPU (quantized there); `wq` keeps a host
+        copy, as the reference's linears hold their packed arrays."""
+        from dataclasses import replace
+        self.d = d
+        host = {f: (None if getattr(d, f) is None else getattr(d, f).cpu().numpy())
+                for f in ("qw", "scales", "zeros", "e8m0") if hasattr(d, f)}
+        self.wq = replace(d, **host)
         self.params = params
-        self.nbytes = wq.nbytes
+        self.nbytes = self.wq.nbytes
 
     def _x(self, x):
         torch = _torch()
@@ -235,7 +243,7 @@ class W4A16Linear(_LowbitLinear):
 
     def __init__(self, w, b=None, threads=None, asym=False, params=None, int4_scale="absmax", **_):
         super().__init__(w, b, threads)
-        self._setup(quantize_int4(np.asarray(w, np.float32), asym=asym, scale=int4_scale), params)
+        self._setup(quantize_int4_cuda(np.asarray(w, np.float32), asym=asym, scale=int4_scale), params)
 
     def mm(self, x):
         torch = _torch()
@@ -249,12 +257,37 @@ class W4A16Linear(_LowbitLinear):
         return y
 
 
+    def mm_rmsnorm(self, x, res, x_out, norm_w, eps: float):
+        """rmsnorm(x + res) @ W.T in one decode kernel (M <= 2); x + res -> x_out."""
+        torch = _torch()
+        m = int(x.shape[0])
+        y = torch.empty((m, self.n), dtype=torch.float32, device=x.device)
+        d = self.d
+        _check(_lib().lbc_gemm_w4a16_rmsnorm(x.data_ptr(), None if res is None else res.data_ptr(),
+                                             None if res is None else x_out.data_ptr(), norm_w.data_ptr(), eps, m,
+                                             self.wq.kp, d.qw.data_ptr(), d.scales.data_ptr(),
+                                             None if d.zeros is None else d.zeros.data_ptr(), self.n, y.data_ptr(),
+                                             self._pparams(m), _stream()), "lbc_gemm_w4a16_rmsnorm")
+        return y
+
+    def mm_glu(self, gu):
+        """(silu(gu[:, :K]) * gu[:, K:]) @ W.T in one decode kernel (M <= 2)."""
+        torch = _torch()
+        m = int(gu.shape[0])
+        y = torch.empty((m, self.n), dtype=torch.float32, device=gu.device)
+        d = self.d
+        _check(_lib().lbc_gemm_w4a16_glu(gu.data_ptr(), m, self.wq.kp, d.qw.data_ptr(), d.scales.data_ptr(),
+                                         None if d.zeros is None else d.zeros.data_ptr(), self.n, y.data_ptr(),
+                                         self._pparams(m), _stream()), "lbc_gemm_w4a16_glu")
+        return y
+
+
 class W4A8Linear(_LowbitLinear):
     kind = "w4a8"
 
     def __init__(self, w, b=None, threads=None, asym=False, params=None, int4_scale="absmax", **_):
         super().__init__(w, b, threads)
-        self._setup(quantize_int4(np.asarray(w, np.float32), asym=asym, scale=int4_scale), params)
+        self._setup(quantize_int4_cuda(np.asarray(w, np.float32), asym=asym, scale=int4_scale), params)
 
     def mm(self, x):
         from .kernels import _workspace
@@ -275,7 +308,7 @@ class MXFP4Linear(_LowbitLinear):
 
     def __init__(self, w, b=None, threads=None, params=None, **_):
         super().__init__(w, b, threads)
-        self._setup(quantize_mxfp4(np.asarray(w, np.float32)), params)
+        self._setup(quantize_mxfp4_cuda(np.asarray(w, np.float32)), params)
 
     def mm(self, x):
         torch = _torch()
@@ -323,6 +356,10 @@ class KVCache:
     def length(self, n: int) -> None:
         self._length = int(n)
         self.pos.fill_(int(n))
+
+    def reset(self) -> None:
+        """Empty the cache (keeps its buffers, so a captured decode graph stays valid)."""
+        self.length = 0
 
 
 @dataclass
@@ -373,6 +410,10 @@ class Model:
         self.lm_head = (lin if quantize_lm_head else FP32Linear)(head, None, **kw)
         cos, sin = rope_tables(cfg.head_dim, cfg.max_position, cfg.rope_theta)
         self.cos, self.sin = to_cuda(cos), to_cuda(sin)
+        # decode steps fuse the norms and the SiLU*up into the w4a16 GEMVs
+        # (default tiling, unpadded hidden and intermediate sizes)
+        self._fusable = (backend == "w4a16" and params is None and cfg.hidden_size % 128 == 0
+                         and cfg.intermediate_size % 128 == 0)
         self._graphs: dict = {}
 
     # ------------------------------------------------------------ bookkeeping
@@ -411,23 +452,44 @@ class Model:
         q = torch.empty((n, H * D), dtype=torch.float32, device=x.device)
         att = torch.empty((n, H * D), dtype=torch.float32, device=x.device)
         m = torch.empty((n, I), dtype=torch.float32, device=x.device)
+        # decode (one or two token rows) with w4a16 linears: the norms and the
+        # SiLU*up run inside the GEMV kernels; the residual stream ping-pongs
+        # between two buffers because the fused kernels read x while writing x + res
+        fuse = self._fusable and n <= 2
+        xb = torch.empty_like(x) if fuse else None
         res = None
         for li, L in enumerate(self.layers):
-            _check(lib.lbc_rmsnorm(x.data_ptr(), None if res is None else res.data_ptr(), x.data_ptr(),
-                                   L.ln1.data_ptr(), h.data_ptr(), n, hid, eps, st), "lbc_rmsnorm")
-            qkv = L.qkv.mm(h)
-            _check(lib.lbc_qkv_rope(qkv.data_ptr(), None if L.qkv.b is None else L.qkv.b.data_ptr(),
-                                    self.cos.data_ptr(), self.sin.data_ptr(), cache.pos.data_ptr(), q.data_ptr(),
-                                    cache.k[li].data_ptr(), cache.v[li].data_ptr(), B, T, H, KV, D, S, st),
-                   "lbc_qkv_rope")
-            _check(lib.lbc_attention(q.data_ptr(), cache.k[li].data_ptr(), cache.v[li].data_ptr(),
-                                     cache.pos.data_ptr(), att.data_ptr(), B, T, H, KV, D, S, st), "lbc_attention")
+            if fuse:
+                qkv = L.qkv.mm_rmsnorm(x, res, xb, L.ln1, eps)
+                if res is not None:
+                    x, xb = xb, x
+            else:
+                _check(lib.lbc_rmsnorm(x.data_ptr(), None if res is None else res.data_ptr(), x.data_ptr(),
+                                       L.ln1.data_ptr(), h.data_ptr(), n, hid, eps, st), "lbc_rmsnorm")
+                qkv = L.qkv.mm(h)
+            bias = None if L.qkv.b is None else L.qkv.b.data_ptr()
+            if T == 1:  # one launch: RoPE, cache append and attention
+                _check(lib.lbc_rope_attention(qkv.data_ptr(), bias, self.cos.data_ptr(), self.sin.data_ptr(),
+                                              cache.pos.data_ptr(), cache.k[li].data_ptr(), cache.v[li].data_ptr(),
+                                              att.data_ptr(), B, H, KV, D, S, st), "lbc_rope_attention")
+            else:
+                _check(lib.lbc_qkv_rope(qkv.data_ptr(), bias, self.cos.data_ptr(), self.sin.data_ptr(),
+                                        cache.pos.data_ptr(), q.data_ptr(), cache.k[li].data_ptr(),
+                                        cache.v[li].data_ptr(), B, T, H, KV, D, S, st), "lbc_qkv_rope")
+                _check(lib.lbc_attention(q.data_ptr(), cache.k[li].data_ptr(), cache.v[li].data_ptr(),
+                                         cache.pos.data_ptr(), att.data_ptr(), B, T, H, KV, D, S, st),
+                       "lbc_attention")
             y = L.o.mm(att)
-            _check(lib.lbc_rmsnorm(x.data_ptr(), y.data_ptr(), x.data_ptr(), L.ln2.data_ptr(), h.data_ptr(),
-                                   n, hid, eps, st), "lbc_rmsnorm")
-            gu = L.gate_up.mm(h)
-            _check(lib.lbc_silu_mul(gu.data_ptr(), m.data_ptr(), n, I, st), "lbc_silu_mul")
-            res = L.down.mm(m)
+            if fuse:
+                gu = L.gate_up.mm_rmsnorm(x, y, xb, L.ln2, eps)
+                x, xb = xb, x
+                res = L.down.mm_glu(gu)
+            else:
+                _check(lib.lbc_rmsnorm(x.data_ptr(), y.data_ptr(), x.data_ptr(), L.ln2.data_ptr(), h.data_ptr(),
+                                       n, hid, eps, st), "lbc_rmsnorm")
+                gu = L.gate_up.mm(h)
+                _check(lib.lbc_silu_mul(gu.data_ptr(), m.data_ptr(), n, I, st), "lbc_silu_mul")
+                res = L.down.mm(m)
         xn = torch.empty_like(h)
         _check(lib.lbc_rmsnorm(x.data_ptr(), res.data_ptr(), x.data_ptr(), self.norm.data_ptr(), xn.data_ptr(),
                                n, hid, eps, st), "lbc_rmsnorm")

@@ -129,3 +129,102 @@ def test_operator_errors():
     assert lib().lbc_qkv_rope(None, None, None, None, None, None, None, None, 1, 1, 3, 2, 64, 16, None) < 0
     assert lib().lbc_rmsnorm(None, None, None, None, None, 1, 0, 1e-6, None) < 0
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("H,KV,D", [(14, 2, 64), (4, 4, 32), (8, 1, 128)])
+def test_fused_rope_attention_equals_separate_kernels(H, KV, D):
+    """lbc_rope_attention (decode steps) = lbc_qkv_rope then lbc_attention, bit for bit."""
+    from lowbit_b200.kernels import lib
+    B, S, pos = 3, 40, 13
+    g = torch.Generator().manual_seed(0)
+    W = (H + 2 * KV) * D
+    qkv = torch.randn(B, W, generator=g).cuda()
+    bias = torch.randn(W, generator=g).cuda()
+    cos, sin = (torch.from_numpy(a).cuda() for a in PM.rope_tables(D, 64, 1e4))
+    kc = torch.randn(B, KV, S, D, generator=g).cuda()
+    vc = torch.randn(B, KV, S, D, generator=g).cuda()
+    k2, v2 = kc.clone(), vc.clone()
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    q = torch.empty(B, H * D, device="cuda")
+    o1, o2 = torch.empty(B, H * D, device="cuda"), torch.empty(B, H * D, device="cuda")
+    L, st = lib(), torch.cuda.current_stream().cuda_stream
+    assert L.lbc_qkv_rope(qkv.data_ptr(), bias.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), q.data_ptr(),
+                          kc.data_ptr(), vc.data_ptr(), B, 1, H, KV, D, S, st) == 0
+    assert L.lbc_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), p.data_ptr(), o1.data_ptr(), B, 1, H, KV, D,
+                           S, st) == 0
+    assert L.lbc_rope_attention(qkv.data_ptr(), bias.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(),
+                                k2.data_ptr(), v2.data_ptr(), o2.data_ptr(), B, H, KV, D, S, st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(kc, k2) and torch.equal(vc, v2)
+    assert torch.equal(o1, o2)
+    # against a float64 evaluation of the same attention
+    qd = q.double().view(B, H, D)
+    kd, vd = kc.double()[:, :, :pos + 1], vc.double()[:, :, :pos + 1]
+    G = H // KV
+    ref = torch.empty(B, H, D, dtype=torch.float64)
+    for b in range(B):
+        for h in range(H):
+            s = (kd[b, h // G] @ qd[b, h]) / np.sqrt(D)
+            ref[b, h] = torch.softmax(s, 0) @ vd[b, h // G]
+    assert float((o1.double().cpu().view(B, H, D) - ref.cpu()).abs().max()) < 1e-4
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1152, 896), (2, 300, 256), (1, 96, 4864), (2, 513, 1024)])
+def test_fused_decode_gemvs_equal_two_kernel_path(m, n, k):
+    """lbc_gemm_w4a16_glu equals lbc_silu_mul + lbc_gemm_w4a16 bit for bit;
+    lbc_gemm_w4a16_rmsnorm equals lbc_rmsnorm + lbc_gemm_w4a16 up to the order
+    of the norm's sum of squares, and stores x + residual."""
+    import ctypes as C
+    from lowbit_b200.kernels import _Params, lib
+    from lowbit_b200.kernels import quantize_int4_cuda
+    L, st = lib(), torch.cuda.current_stream().cuda_stream
+    g = torch.Generator().manual_seed(m * 7 + n)
+    W = quantize_int4_cuda(torch.randn(n, k, generator=g), asym=True)
+    args = (W.qw.data_ptr(), W.scales.data_ptr(), W.zeros.data_ptr(), n)
+    P = C.byref(_Params(-1, 0, 0, 0, 0, 0, 0))
+    # GLU
+    gu = torch.randn(m, 2 * k, generator=g).cuda()
+    mid = torch.empty(m, k, device="cuda")
+    y1, y2 = torch.empty(m, n, device="cuda"), torch.empty(m, n, device="cuda")
+    assert L.lbc_silu_mul(gu.data_ptr(), mid.data_ptr(), m, k, st) == 0
+    assert L.lbc_gemm_w4a16(mid.data_ptr(), m, k, *args, y1.data_ptr(), P, st) >= 0
+    assert L.lbc_gemm_w4a16_glu(gu.data_ptr(), m, k, *args, y2.data_ptr(), P, st) >= 0
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    # RMSNorm with a residual
+    x = torch.randn(m, k, generator=g).cuda()
+    r = torch.randn(m, k, generator=g).cuda()
+    w = (1 + 0.1 * torch.randn(k, generator=g)).cuda()
+    xs, h = x.clone(), torch.empty(m, k, device="cuda")
+    xo = torch.empty(m, k, device="cuda")
+    assert L.lbc_rmsnorm(xs.data_ptr(), r.data_ptr(), xs.data_ptr(), w.data_ptr(), h.data_ptr(), m, k, 1e-6, st) == 0
+    assert L.lbc_gemm_w4a16(h.data_ptr(), m, k, *args, y1.data_ptr(), P, st) >= 0
+    assert L.lbc_gemm_w4a16_rmsnorm(x.data_ptr(), r.data_ptr(), xo.data_ptr(), w.data_ptr(), 1e-6, m, k, *args,
+                                    y2.data_ptr(), P, st) >= 0
+    torch.cuda.synchronize()
+    assert torch.equal(xo, xs)
+    scale = float(y1.abs().max())
+    assert float((y1 - y2).abs().max()) <= 1e-5 * scale
+    # no residual: x as given, x_out untouched
+    assert L.lbc_gemm_w4a16_rmsnorm(x.data_ptr(), None, None, w.data_ptr(), 1e-6, m, k, *args, y2.data_ptr(), P,
+                                    st) >= 0
+    assert L.lbc_rmsnorm(x.data_ptr(), None, None, w.data_ptr(), h.data_ptr(), m, k, 1e-6, st) == 0
+    assert L.lbc_gemm_w4a16(h.data_ptr(), m, k, *args, y1.data_ptr(), P, st) >= 0
+    torch.cuda.synchronize()
+    assert float((y1 - y2).abs().max()) <= 1e-5 * float(y1.abs().max())
+
+
+def test_fused_decode_gemv_rejects_ineligible_calls():
+    import ctypes as C
+    from lowbit_b200.kernels import _Params, lib
+    L = lib()
+    P = C.byref(_Params(-1, 0, 0, 0, 0, 0, 0))
+    x = torch.zeros(3, 256, device="cuda")
+    q = torch.zeros(8, 128, dtype=torch.uint8, device="cuda")
+    s = torch.ones(8, 2, device="cuda")
+    y = torch.empty(3, 8, device="cuda")
+    # three tokens: not a decode shape
+    assert L.lbc_gemm_w4a16_glu(x.data_ptr(), 3, 128, q.data_ptr(), s.data_ptr(), None, 8, y.data_ptr(), P, None) == -2
+    # x_out aliasing x
+    assert L.lbc_gemm_w4a16_rmsnorm(x.data_ptr(), x.data_ptr(), x.data_ptr(), s.data_ptr(), 1e-6, 1, 256,
+                                    q.data_ptr(), s.data_ptr(), None, 8, y.data_ptr(), P, None) == -1
