@@ -331,13 +331,20 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *o
 // Kernel path: explicit requests are honoured; automatic selection sends one
 // or two tokens to the register-streamed decode kernel and three or more to
 // the tensor-core kernel (W4A8 from 32 tokens: below that its int32 dp4a SIMT
-// kernel is faster).
-bool want_tc(const lbc_params *p, int fmt, int M) {
+// kernel is faster), except small matrices below 32 tokens: the tensor-core
+// path's fixed cost (activation-block kernel, TMEM and pipeline set-up, about
+// 10-18 us on B200) exceeds the SIMT kernels' time there (measured: N*Kp below
+// 10M weights up to 4 tokens, below 6M up to 31).
+bool want_tc(const lbc_params *p, int fmt, int M, int N, int Kp) {
   if (p && p->isa == LBC_PATH_TCGEN05) return true;
   const bool automatic = !p || p->isa == LBC_PATH_AUTO || p->isa >= 2;
   if (!automatic) return false;
   if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
-  return fmt == lbc::FMT_W4A8 ? M >= 32 : M >= 3;
+  if (fmt == lbc::FMT_W4A8) return M >= 32;
+  if (M < 3) return false;
+  const double w = (double)N * Kp;
+  if (M < 32 && w < (M <= 4 ? 10e6 : 6e6)) return false;
+  return true;
 }
 
 // bf16 prefill kernel (4e-3 tolerance, the north-star prefill contract) from
@@ -395,7 +402,7 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
   if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
   if (int rc = device_gate()) return rc;
   const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
-  if (want_tc(p, fmt, M)) {
+  if (want_tc(p, fmt, M, N, Kp)) {
     if (buf && buflen > 0)
       snprintf(buf, (size_t)buflen, "{\"path\": \"tcgen05\", \"kernel\": \"%s\"}",
                want_prefill(p, fmt, M) ? "prefill" : "tcgemm");
@@ -430,7 +437,7 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
-  if (want_tc(p, lbc::FMT_W4A16, M)) {
+  if (want_tc(p, lbc::FMT_W4A16, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A16; c.x = x; c.qw = qw; c.scales = scales; c.zeros = zeros; c.y = y;
     c.M = M; c.N = N; c.Kp = Kp;
@@ -489,7 +496,7 @@ int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8
   if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
-  if (want_tc(p, lbc::FMT_MXFP4, M)) {
+  if (want_tc(p, lbc::FMT_MXFP4, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_MXFP4; c.x = x; c.qw = qw; c.e8m0 = e8m0; c.y = y;
     c.M = M; c.N = N; c.Kp = Kp;
@@ -520,7 +527,7 @@ int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int 
   if (!xq || !xs || !asum || !qw || !scales || !y || !al16(xq) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
-  if (want_tc(p, lbc::FMT_W4A8, M)) {
+  if (want_tc(p, lbc::FMT_W4A8, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
@@ -566,7 +573,7 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
   int rc = 0;
   cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, st);
   if (e != cudaSuccess) rc = fail_cuda("quant_act_int8 launch", e);
-  if (rc == 0 && want_tc(p, lbc::FMT_W4A8, M)) {
+  if (rc == 0 && want_tc(p, lbc::FMT_W4A8, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;

@@ -149,11 +149,19 @@ def _path_id(isa) -> int:
     return PATH_IDS[isa]
 
 
-def effective_isa(kind: str, isa=None, m: int = 1) -> str:
-    """Kernel path a GEMM of `kind` with `m` tokens and default params runs on."""
+def effective_isa(kind: str, isa=None, m: int = 1, n: int | None = None, k: int | None = None) -> str:
+    """Kernel path a GEMM of `kind` with `m` tokens (and an n x k weight, when
+    given) runs on with default params; the library's rule (capi.cu want_tc)."""
     pid = _path_id(isa)
     if pid == -1:
-        pid = 1 if m >= (32 if kind == "w4a8" else 3) else 0
+        if kind == "w4a8":
+            pid = 1 if m >= 32 else 0
+        elif m < 3:
+            pid = 0
+        elif n is not None and k is not None and m < 32 and n * pad_to(k, GROUP) < (10e6 if m <= 4 else 6e6):
+            pid = 0
+        else:
+            pid = 1
     return PATHS[pid]
 
 

@@ -52,7 +52,7 @@ def save_cache(data: dict, path: Path | str = DEFAULT_CACHE) -> None:
 def lookup(kind: str, m: int, n: int, k: int, isa=None,
            path: Path | str = DEFAULT_CACHE) -> K.Params | None:
     try:
-        e = load_cache(path)["entries"].get(key(kind, m, n, k, K.effective_isa(kind, isa, m)))
+        e = load_cache(path)["entries"].get(key(kind, m, n, k, K.effective_isa(kind, isa, m, n, k)))
     except (OSError, ValueError):
         return None
     return K.Params(**e["params"]) if e else None
