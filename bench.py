@@ -20,6 +20,13 @@ Reference arm: lowbit's own CPU kernels (compiled from the reference's sources
 into oracle/_ref) on all host cores, same config, same metric.
 
     python bench.py --workload model [--steps K] [--warmup W]
+    python bench.py --workload gemm --fmt w4a16|w4a8|mxfp4 --m M --n N --k K
+    python bench.py --workload sweep
+
+GEMM workloads: one GEMM per step on seeded inputs (the BASELINE shape sweep
+of configs[3] for `sweep`), weights quantized on the GPU, a CUDA graph of the
+steps over rotating weight copies; each line carries its roofline (tensor or
+HBM, whichever bounds the shape).
 
 Model workload: the Qwen2-0.5B-shaped decoder (24
 layers, hidden 896, 14/2 heads, SwiGLU 4864, vocabulary 151936, tied
@@ -422,6 +429,86 @@ def _ncu_traffic(workload: str):
         return None
 
 
+# ---------------------------------------------------------------- GEMM workloads (BASELINE configs[1..3])
+SWEEP_M = (1, 16, 64, 512, 4096)
+SWEEP_NK = ((4096, 4096), (11008, 4096), (4096, 11008), (14336, 4096))
+
+
+def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int) -> dict:
+    """One GEMM of `fmt` (w4a16 asym / w4a8 sym / mxfp4) on seeded N(0,1) inputs,
+    device-resident, timed as a CUDA graph of `steps` calls over rotating
+    weight copies (inputs + copies larger than L2), CUDA events."""
+    import torch
+    from lowbit_b200 import kernels as Kn
+    from lowbit_b200.kernels import quantize_int4_cuda, quantize_mxfp4_cuda
+    hbm, tf_burst, tf_sust, src = peaks()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = torch.randn(n, k, device="cuda", generator=g)
+    x = torch.randn(m, k, device="cuda", generator=g)
+    W = (quantize_mxfp4_cuda(w) if fmt == "mxfp4" else quantize_int4_cuda(w, asym=(fmt == "w4a16")))
+    del w
+    wbytes = int(sum(t.numel() * t.element_size() for t in
+                     ((W.qw, W.e8m0) if fmt == "mxfp4" else (W.qw, W.scales, W.zeros)) if t is not None))
+    copies = int(max(1, min(16, np.ceil(2 * L2_BYTES / max(1, wbytes + 4 * m * (k + n))))))
+    from dataclasses import replace
+    pool = [W] + [replace(W, **{f: getattr(W, f).clone() for f in ("qw", "scales", "zeros", "e8m0")
+                                if getattr(W, f, None) is not None}) for _ in range(copies - 1)]
+    fn = {"w4a16": Kn.gemm_w4a16, "w4a8": Kn.gemm_w4a8, "mxfp4": Kn.gemm_mxfp4}[fmt]
+    prep = Kn._Prepared(x, W.kp, n)
+    for i in range(warmup):
+        fn(x, pool[i % copies], _prep=prep)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            fn(x, pool[i % copies], _prep=prep)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    flops = 2.0 * m * n * k
+    byts = wbytes + 4 * m * W.kp + 4 * m * n
+    peak_t = tf_burst * (2 if fmt == "w4a8" else 1)
+    tensor_bound = flops / (peak_t * 1e12) > byts / (hbm * 1e9)
+    plan = Kn.describe_plan(fmt, m, n, W.kp)
+    ach = flops / us / 1e6 if tensor_bound else byts / us / 1e3
+    peak = peak_t if tensor_bound else hbm
+    return {"fmt": fmt, "M": m, "N": n, "K": k, "us": round(us, 3), "TFLOP/s": round(flops / us / 1e6, 2),
+            "GB/s": round(byts / us / 1e3, 1), "kernel": plan.get("kernel", plan.get("path")),
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": round(ach, 2),
+                         "peak": peak, "unit": "TFLOP/s" if tensor_bound else "GB/s", "frac": round(ach / peak, 4),
+                         "peak_source": src + (" (int8: 2x the bf16 figure, not measured)"
+                                               if tensor_bound and fmt == "w4a8" else "")},
+            "weight_copies": copies}
+
+
+def run_gemm(args) -> dict:
+    line = gemm_line(args.fmt, args.m, args.n, args.k, args.steps, args.warmup)
+    return {"metric": f"{args.fmt} GEMM time (M={args.m}, N={args.n}, K={args.k})", "value": line["us"],
+            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": line["us"] / 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"w4a16": "f32 (bf16 from 64 tokens)", "w4a8": "int8/int32",
+                      "mxfp4": "f32 (bf16 from 64 tokens)"}[args.fmt],
+            "data": "synthetic: W, X ~ N(0,1) (torch seed 0), quantized on the GPU",
+            "config": {"workload": f"{args.fmt} GEMM M={args.m} N={args.n} K={args.k}",
+                       "timing": "CUDA graph of `steps` calls over rotating weight copies, CUDA events"},
+            "detail": line}
+
+
+def run_sweep(args) -> dict:
+    rows = []
+    for fmt in ("w4a16", "w4a8", "mxfp4"):
+        for m in SWEEP_M:
+            for n, k in SWEEP_NK:
+                steps = max(3, min(args.steps, int(2e6 / (m * n * k / 1e6 + 50))))
+                rows.append(gemm_line(fmt, m, n, k, steps, 3))
+    return {"metric": "GEMM shape sweep (BASELINE configs[3], 1 GPU)", "rows": rows}
+
+
 # ---------------------------------------------------------------- model workload
 MODEL_METRIC = "Qwen2-0.5B-shape greedy decode tokens/s (w4a16 int4-g128 asym, batch 1)"
 
@@ -527,10 +614,17 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["decode", "model"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "model", "gemm", "sweep"], default="decode")
+    ap.add_argument("--fmt", choices=["w4a16", "w4a8", "mxfp4"], default="w4a16")
+    ap.add_argument("--m", type=int, default=4096)
+    ap.add_argument("--n", type=int, default=11008)
+    ap.add_argument("--k", type=int, default=4096)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload in ("gemm", "sweep"):
+        print(json.dumps(run_gemm(args) if args.workload == "gemm" else run_sweep(args)), flush=True)
+        return
     if args.workload == "model":
         if args.steps > 50:
             args.steps = 3  # a step is a whole 128-token generation here

@@ -347,10 +347,13 @@ bool want_tc(const lbc_params *p, int fmt, int M, int N, int Kp) {
   return true;
 }
 
-// bf16 prefill kernel (4e-3 tolerance, the north-star prefill contract) from
-// 64 tokens unless tokens per pass (mr) are given, which keeps the exact kernel
+// prefill kernel (128-token tiles) from 64 tokens unless tokens per pass (mr)
+// are given, which keeps the exact kernel: W4A16 / MXFP4 with bf16
+// activations (4e-3 tolerance, the north-star prefill contract), W4A8 with
+// int8 activations and exact int32 group sums (no extra tolerance)
 bool want_prefill(const lbc_params *p, int fmt, int M) {
-  return fmt != lbc::FMT_W4A8 && M >= 64 && !(p && p->mr > 0);
+  (void)fmt;
+  return M >= 64 && !(p && p->mr > 0);
 }
 
 int run_tc(lbc::TcCall c, cudaStream_t st) {
@@ -531,6 +534,7 @@ int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int 
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
+    c.prefill = want_prefill(p, c.fmt, M);
     return run_tc(c, static_cast<cudaStream_t>(stream));
   }
   lbc::GemvArgs a{};
@@ -577,6 +581,7 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;
+    c.prefill = want_prefill(p, c.fmt, M);
     c.scratch = ws + off_tc;
     c.scratch_bytes = bytes - off_tc;
     rc = run_tc(c, st);

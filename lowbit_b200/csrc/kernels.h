@@ -32,7 +32,7 @@ struct TcCall {
   size_t scratch_bytes;
   int *status;
   int sms, smem_optin;
-  int prefill;             // 1: bf16 prefill kernel (W4A16 / MXFP4, 4e-3 tolerance), 0: exact kernel
+  int prefill;             // 1: 128-token prefill kernel (bf16 W4A16 / MXFP4: 4e-3 tolerance; W4A8 exact), 0: exact kernel
 };
 // scratch for format `fmt` (FMT_* id), M tokens, Kp columns when the grid
 // has `ctas` CTAs (at most the SM count)

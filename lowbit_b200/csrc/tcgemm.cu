@@ -1,3 +1,4 @@
+#include <algorithm>
 // Tensor-core GEMM: instantiations, planning and launch (see tcgemm.cuh).
 #include <atomic>
 #include <chrono>
@@ -31,7 +32,11 @@ size_t scratch_bytes(int fmt, int M, int Kp, int ctas) {
   const size_t flags = round256(chunks * ctas * sizeof(uint32_t));
   const size_t nkb = (size_t)((Kp + TC_KB - 1) / TC_KB);
   const size_t bglob = tc_btma(mt) ? round256(chunks * nkb * tc_bblock(fmt, mt)) : 0;
-  return part + flags + bglob;
+  // 64+ tokens may take the prefill kernel instead: its activation blocks
+  const size_t pf = M >= 64 ? round256((size_t)((M + PF_TOK - 1) / PF_TOK) * nkb * tc_nmma(PF_TOK, 1) * 256 *
+                                       (fmt == FMT_W4A8 ? 1 : 2))
+                            : 0;
+  return std::max(part + flags + bglob, pf);
 }
 
 // A value no earlier call in this process used: partial-tile flags carry it.
@@ -102,12 +107,15 @@ size_t tc_scratch_bytes(int fmt, int M, int Kp, int ctas) { return scratch_bytes
 
 namespace {
 
-// Prefill: activation blocks [token chunks][K blocks][128 rows x 256 K bf16]
+// Prefill: activation blocks [token chunks][K blocks][128 rows x 256 K bf16 or
+// int8]
 // in the scratch, then the prefill kernel over (128-row, 128-token) tiles.
 int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   const int fmt = c.fmt;
   TcArgs a{};
   a.x = c.x;
+  a.xq = c.xq;
+  a.xs = c.xs;
   a.scales = c.scales;
   a.zeros = c.zeros;
   a.e8m0 = c.e8m0;
@@ -120,7 +128,7 @@ int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   a.ntiles = (c.N + TC_ROWS - 1) / TC_ROWS;
   const int nch = (c.M + PF_TOK - 1) / PF_TOK;
   a.units = a.ntiles * nch;
-  a.b_block_bytes = tc_nmma(PF_TOK, 1) * 256 * 2;
+  a.b_block_bytes = tc_nmma(PF_TOK, 1) * 256 * (fmt == FMT_W4A8 ? 1 : 2);
   a.status = c.status;
   int stages = 4;
   while (stages > 2 && tc_smem_layout(stages, a.b_block_bytes, PF_TOK).total > c.smem_optin) --stages;
@@ -138,14 +146,16 @@ int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   }
   const size_t need = round256((size_t)nch * a.nkb * a.b_block_bytes);
   bool owned = false;
-  uint8_t *scr = static_cast<uint8_t *>(cached_scratch(need, st, &owned));
+  uint8_t *scr = static_cast<uint8_t *>(c.scratch);  // a caller's workspace, when large enough
+  if (!scr || c.scratch_bytes < need) scr = static_cast<uint8_t *>(cached_scratch(need, st, &owned));
   if (!scr) {
     snprintf(err, errlen, "allocation of %zu bytes of GEMM scratch failed", need);
     return LBC_ERR_ALLOC;
   }
   a.bglob = scr;
-  cudaError_t e = fmt == FMT_W4A16 ? tc_prefill_launch<FMT_W4A16>(map, a, nch, grid_x, smem, st)
-                                   : tc_prefill_launch<FMT_MXFP4>(map, a, nch, grid_x, smem, st);
+  cudaError_t e = fmt == FMT_W4A16  ? tc_prefill_launch<FMT_W4A16>(map, a, nch, grid_x, smem, st)
+                   : fmt == FMT_W4A8 ? tc_prefill_launch<FMT_W4A8>(map, a, nch, grid_x, smem, st)
+                                     : tc_prefill_launch<FMT_MXFP4>(map, a, nch, grid_x, smem, st);
   if (owned) cudaFreeAsync(scr, st);
   if (e != cudaSuccess) {
     snprintf(err, errlen, "tensor-core prefill launch: %s%s", cudaGetErrorString(e), tc_launch_note());
@@ -157,7 +167,7 @@ int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
 }  // namespace
 
 int tc_gemm(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
-  if (c.prefill && c.fmt != FMT_W4A8) return tc_prefill(c, st, err, errlen);
+  if (c.prefill) return tc_prefill(c, st, err, errlen);
   const int fmt = c.fmt;
   const int mt = tc_mt(c.M);
   const int chunks = (c.M + mt - 1) / mt;

@@ -1,6 +1,6 @@
 // Tensor-core prefill GEMM (tcgen05, sm_100a) for many tokens.
 //
-// Y[M,N] = X[M,K] . W[N,K]^T, W4A16 and MXFP4. An output tile is 128 weight
+// Y[M,N] = X[M,K] . W[N,K]^T, W4A16, MXFP4 and W4A8. An output tile is 128 weight
 // rows (the MMA's M) x 128 tokens (its N); a persistent CTA walks its tiles
 // and, per tile, the 256-K units of the row, two 128-element groups each:
 //
@@ -12,6 +12,11 @@
 //     fp32 to each group's accumulator, so the only rounding is that of X
 //     (|error| <= 2^-8 * (|X| . |W|^T)); MXFP4: A = e2m1(q) * 2^(e-127), exact
 //     in bf16, scale 1;
+//   * W4A8 (kind::i8): A = q - z as s8 (|q - z| <= 15), B = the per-token int8
+//     activations, so each group's int32 accumulator is exactly the
+//     reference's sum(q * a) - z * sum(a); the epilogue converts it exactly
+//     (|acc| < 2^22) and applies the group scale in fp32, the token scale xs
+//     at the store -- no tolerance beyond the reference's own;
 //   * TMEM (512 columns): the unit's two A groups [0, 128) and a ring of
 //     three per-group accumulators D [128, 512). The MMAs of the next groups
 //     run while the epilogue warps fold D_g * s_g into their running sums,
@@ -36,12 +41,13 @@ constexpr int PF_THREADS = 480;  // 4 dequantising + producer + 2 MMA + 8 epilog
 
 template <int FMT>
 __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtensorMap wmap, const TcArgs a) {
-  static_assert(FMT == FMT_W4A16 || FMT == FMT_MXFP4, "bf16 formats");
+  constexpr bool I8 = (FMT == FMT_W4A8);
   constexpr int NMMA = PF_TOK;
-  constexpr int GCOLS = 64, HCOLS = 32;  // TMEM columns per (row, group) / half group
-  constexpr int DCOL0 = 128, NDR = 3;    // accumulator ring
-  constexpr int NSTEP = 8;               // K=16 MMAs per group
-  constexpr int SBO = 4096;              // bytes between 8-row groups of B
+  constexpr int GCOLS = I8 ? 32 : 64, HCOLS = GCOLS / 2;  // TMEM columns per (row, group) / half group
+  constexpr int DCOL0 = 128, NDR = 3;                      // accumulator ring
+  constexpr int NSTEP = I8 ? 4 : 8;                        // K=32 (i8) or K=16 (bf16) MMAs per group
+  constexpr int EPR = I8 ? 16 : 8;                         // B elements per 16-byte core-matrix row
+  constexpr int SBO = TC_KB / EPR * 128;                   // bytes between 8-row groups of B
   constexpr int NDQ = 4;
   constexpr int W_PROD = NDQ, W_MMA = NDQ + 1, W_EPI = NDQ + 3, NEPI = 8;
   constexpr int ECOLS = NMMA / 2;        // token columns per epilogue thread
@@ -145,8 +151,8 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
     // ------------------------------------------------------------ MMA issuers (one per group)
     if (lane == 0) {
       const int h = warp - W_MMA;
-      const uint32_t idesc = tc::idesc_bf16_f32(NMMA);
-      const uint32_t hoff = (uint32_t)(128 * h) / 8u * 128u;
+      const uint32_t idesc = I8 ? tc::idesc_s8_s32(NMMA) : tc::idesc_bf16_f32(NMMA);
+      const uint32_t hoff = (uint32_t)(128 * h) / (uint32_t)EPR * 128u;
       int s = 0, d = h, dr = 0;  // group sequence v = 2i + h: slot v % 3, round v / 3
       uint32_t ph = 0;
       for (int i = 0; i < nunits && !*abort_flag; ++i) {
@@ -160,7 +166,12 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
         const uint32_t dcol = tmem + DCOL0 + d * NMMA;
         const uint32_t acol0 = tmem + h * GCOLS;
 #pragma unroll
-        for (int j = 0; j < NSTEP; ++j) tc::mma_bf16_ts(dcol, acol0 + 8 * j, bd0 + 16u * j, idesc, j > 0);
+        for (int j = 0; j < NSTEP; ++j) {
+          if (I8)
+            tc::mma_s8_ts(dcol, acol0 + 8 * j, bd0 + 16u * j, idesc, j > 0);
+          else
+            tc::mma_bf16_ts(dcol, acol0 + 8 * j, bd0 + 16u * j, idesc, j > 0);
+        }
         tc::commit(&d_full[d]);
         tc::commit(&a_empty[h]);
         tc::commit(&empty[s]);
@@ -261,6 +272,14 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
           const uint4 wh[2] = {wcur[4 * g + 2 * hf], wcur[4 * g + 2 * hf + 1]};
           if (FMT == FMT_W4A16) {
             deq_w4a16(wh, mcur.z[g], av, MAG);
+          } else if (FMT == FMT_W4A8) {
+            // u8 codes, then q - z as s8 bytes: q + (128 - z) stays below 256 in
+            // every byte (no carry between bytes), and flipping bit 7 maps it
+            // to the two's complement of q - z
+            deq_w4a8(wh, av);
+            const uint32_t zc = (128u - mcur.z[g]) * 0x01010101u;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) av[c] = (av[c] + zc) ^ 0x80808080u;
           } else {
             const uint32_t e2[2] = {mcur.e2[4 * g + 2 * hf], mcur.e2[4 * g + 2 * hf + 1]};
             deq_mxfp4(wh, e2, av);
@@ -269,7 +288,7 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
             const uint32_t at = tmem + lane_base + g * GCOLS + hf * HCOLS;
             uint32_t part[16];
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            for (int c = 0; c < HCOLS / 16; ++c) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) part[j] = av[16 * c + j];
               tc::st16(at + 16 * c, part);
@@ -346,7 +365,13 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
             tc::ld8(tmem + lane_base + DCOL0 + d * NMMA + ch * ECOLS + 8 * c, dv);
             tc::wait_ld();
 #pragma unroll
-            for (int j = 0; j < 8; ++j) yacc[8 * c + j] = fmaf(__uint_as_float(dv[j]), sc, yacc[8 * c + j]);
+            for (int j = 0; j < 8; ++j) {
+              // int32 accumulator to fp32 exactly: |acc| < 2^22, so 1.5 * 2^23 + acc
+              // is an fp32 with acc in its low mantissa bits
+              const float dvf = I8 ? __fsub_rn(__int_as_float((int)dv[j] + 0x4B400000), 12582912.0f)
+                                   : __uint_as_float(dv[j]);
+              yacc[8 * c + j] = fmaf(dvf, sc, yacc[8 * c + j]);
+            }
           }
         }
         tc::fence_before_sync();
@@ -366,7 +391,7 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
           const int mlim = a.M - m0;
 #pragma unroll
           for (int j = 0; j < ECOLS; ++j) {
-            if (j < mlim) *yp = yacc[j];
+            if (j < mlim) *yp = I8 ? yacc[j] * __ldg(a.xs + m0 + j) : yacc[j];
             yp += a.N;
           }
         }
