@@ -33,8 +33,11 @@ size_t scratch_bytes(int fmt, int M, int Kp, int ctas) {
   const size_t nkb = (size_t)((Kp + TC_KB - 1) / TC_KB);
   const size_t bglob = tc_btma(mt) ? round256(chunks * nkb * tc_bblock(fmt, mt)) : 0;
   // 64+ tokens may take the prefill kernel instead: its activation blocks
+  // (activation blocks, plus split-K partial tiles: at most one 128 x 128
+  // fp32 tile per SM)
   const size_t pf = M >= 64 ? round256((size_t)((M + PF_TOK - 1) / PF_TOK) * nkb * tc_nmma(PF_TOK, 1) * 256 *
-                                       (fmt == FMT_W4A8 ? 1 : 2))
+                                       (fmt == FMT_W4A8 ? 1 : 2)) +
+                                  round256((size_t)ctas * TC_ROWS * PF_TOK * sizeof(float))
                             : 0;
   return std::max(part + flags + bglob, pf);
 }
@@ -138,13 +141,23 @@ int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
     snprintf(err, errlen, "prefill tile does not fit in shared memory");
     return LBC_ERR_PARAMS;
   }
-  const int grid_x = a.units < c.sms ? a.units : c.sms;
+  // split K when the output tiles cannot fill the GPU (few weight-row tiles
+  // at 64-512 tokens): every split keeps at least one 256-K unit
+  // (at most one item per SM, so no CTA runs two)
+  a.ksplit = 1;
+  if (2 * a.units <= c.sms) a.ksplit = std::min(a.nkb, c.sms / a.units);
+  const int items = a.units * a.ksplit;
+  const int grid_x = items < c.sms ? items : c.sms;
   CUtensorMap map;
   if (make_weight_map(&map, c.qw, c.N, c.Kp) != cudaSuccess) {
     snprintf(err, errlen, "cuTensorMapEncodeTiled failed for the weight tensor");
     return LBC_ERR_CUDA;
   }
-  const size_t need = round256((size_t)nch * a.nkb * a.b_block_bytes);
+  // scratch: activation blocks, then (split-K) one partial tile per work item
+  // [items][128 tokens][128 rows] fp32
+  const size_t bglob_bytes = round256((size_t)nch * a.nkb * a.b_block_bytes);
+  const size_t part_bytes = a.ksplit > 1 ? round256((size_t)items * TC_ROWS * PF_TOK * sizeof(float)) : 0;
+  const size_t need = bglob_bytes + part_bytes;
   bool owned = false;
   uint8_t *scr = static_cast<uint8_t *>(c.scratch);  // a caller's workspace, when large enough
   if (!scr || c.scratch_bytes < need) scr = static_cast<uint8_t *>(cached_scratch(need, st, &owned));
@@ -153,6 +166,7 @@ int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
     return LBC_ERR_ALLOC;
   }
   a.bglob = scr;
+  if (a.ksplit > 1) a.partial = reinterpret_cast<float *>(scr + bglob_bytes);
   cudaError_t e = fmt == FMT_W4A16  ? tc_prefill_launch<FMT_W4A16>(map, a, nch, grid_x, smem, st)
                    : fmt == FMT_W4A8 ? tc_prefill_launch<FMT_W4A8>(map, a, nch, grid_x, smem, st)
                                      : tc_prefill_launch<FMT_MXFP4>(map, a, nch, grid_x, smem, st);

@@ -72,6 +72,7 @@ struct TcArgs {
   int units;             // ntiles * nkb
   int stages;
   int b_block_bytes;     // bytes of one activation block in shared memory
+  int ksplit;            // prefill: K ranges per output tile (>= 1; > 1 adds into a zeroed Y)
   int *status;
 };
 

@@ -90,14 +90,15 @@ cudaError_t tc_prefill_launch(const CUtensorMap &map, const TcArgs &a, int nch, 
                                st, a.x, a.xq, const_cast<uint8_t *>(a.bglob), a.M, a.Kp, a.nkb, a.b_block_bytes);
     if (e != cudaSuccess) return e;
   }
-  auto k = tcprefill_kernel<FMT>;
-  static int enabled[64] = {0};
+  auto k = a.ksplit > 1 ? tcprefill_kernel<FMT, true> : tcprefill_kernel<FMT, false>;
+  static int enabled[2][64] = {{0}};
+  const int sk = a.ksplit > 1 ? 1 : 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && enabled[dev] < smem) {
+  if (dev >= 0 && dev < 64 && enabled[sk][dev] < smem) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    enabled[dev] = smem;
+    enabled[sk][dev] = smem;
   }
   cudaError_t e = launch_pdl(k, dim3(grid_x, 1, 1), dim3(PF_THREADS, 1, 1), (size_t)smem, st, map, a);
   if (e != cudaSuccess) {
@@ -105,7 +106,12 @@ cudaError_t tc_prefill_launch(const CUtensorMap &map, const TcArgs &a, int nch, 
     if (cudaFuncGetAttributes(&fa, k) == cudaSuccess)
       snprintf(tc_launch_note(), 160, " [prefill regs=%d maxThreadsPerBlock=%d smem=%d stages=%d]", fa.numRegs,
                fa.maxThreadsPerBlock, smem, a.stages);
+    return e;
   }
+  if (a.ksplit > 1)
+    e = launch_pdl(tc_split_reduce_kernel, dim3(a.units, PF_TOK, 1), dim3(TC_ROWS, 1, 1), (size_t)0, st,
+                   (const float *)a.partial, FMT == FMT_W4A8 ? a.xs : (const float *)nullptr, a.y, a.M, a.N, nch,
+                   a.ksplit);
   return e;
 }
 

@@ -39,7 +39,9 @@ namespace lbc {
 constexpr int PF_TOK = 128;     // tokens per tile (MMA N)
 constexpr int PF_THREADS = 480;  // 4 dequantising + producer + 2 MMA + 8 epilogue warps
 
-template <int FMT>
+// SPLIT: the split-K instantiation (a.ksplit > 1); without it the K range of
+// an item is the whole row and the position bookkeeping folds away
+template <int FMT, bool SPLIT>
 __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtensorMap wmap, const TcArgs a) {
   constexpr bool I8 = (FMT == FMT_W4A8);
   constexpr int NMMA = PF_TOK;
@@ -67,19 +69,37 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nch = (a.M + PF_TOK - 1) / PF_TOK;  // token chunks
   const int ntile = a.ntiles * nch;             // output tiles
-  const int my_tiles = blockIdx.x < ntile ? (ntile - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int nunits = my_tiles * a.nkb;
+  // work items: tile t split into KS contiguous K ranges (split-K when the
+  // tiles alone cannot fill the GPU): each split stores its partial tile to a
+  // workspace slot and tc_split_reduce_kernel adds the slots in split order
+  // (deterministic; no CTA waits on another)
+  const int KS = SPLIT ? a.ksplit : 1;
+  const int nitem = ntile * KS;
 
-  // position of a unit: tile index t (n tile t / nch, token chunk t % nch), K block kb
+  // position of a unit: tile t (n tile t / nch, token chunk t % nch), K block
+  // kb, the end of its item's K range, the item's split index
   struct Pos {
-    int t, kb;
+    int t, kb, khi, sp;
+  };
+  auto start = [&](int w) {
+    const int sp = w % KS;
+    return Pos{w / KS, sp * a.nkb / KS, (sp + 1) * a.nkb / KS, sp};
   };
   auto advance = [&](Pos &p) {
-    if (++p.kb == a.nkb) {
-      p.kb = 0;
-      p.t += gridDim.x;
+    if constexpr (SPLIT) {
+      if (++p.kb == p.khi) p = start(p.t * KS + p.sp + gridDim.x);
+    } else {
+      if (++p.kb == a.nkb) {
+        p.kb = 0;
+        p.t += gridDim.x;
+      }
     }
   };
+  int nunits = 0;
+  for (int w = blockIdx.x; w < nitem; w += gridDim.x) {
+    const Pos p = start(w);
+    nunits += p.khi - p.kb;
+  }
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -114,7 +134,7 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
       const uint64_t pol = policy_evict_first();
       const uint32_t txb = (uint32_t)TC_WBYTES + (uint32_t)a.b_block_bytes;
       const int pro = min(S, nunits);
-      Pos p{(int)blockIdx.x, 0};
+      Pos p = start(blockIdx.x);
       // weights are static: stream them before the previous kernel finishes
       for (int i = 0; i < pro; ++i) {
         mbar_expect_tx(&full[i], txb);
@@ -123,7 +143,7 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
       }
       // the activation blocks come from the preparation kernel before this one
       pdl_wait_prior_grid();
-      Pos pb{(int)blockIdx.x, 0};
+      Pos pb = start(blockIdx.x);
       for (int i = 0; i < pro; ++i) {
         bulk_g2s(smem + L.b_off + i * BSTRIDE, a.bglob + ((size_t)(pb.t % nch) * a.nkb + pb.kb) * a.b_block_bytes,
                  (uint32_t)a.b_block_bytes, &full[i], pol);
@@ -225,7 +245,7 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
       return m;
     };
     // metadata through a 2-deep register queue (loads for unit i + 2)
-    Pos pq{(int)blockIdx.x, 0};
+    Pos pq = start(blockIdx.x);
     Meta mq[2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -331,14 +351,14 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
                                    : ((p.t < ntile && n < a.N && gi < a.G) ? __ldg(a.scales + (size_t)n * a.G + gi) : 0.f);
       }
     };
-    Pos pq{(int)blockIdx.x, 0};
+    Pos pq = start(blockIdx.x);
     float sq[2][2];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       load_scales(pq, sq[j]);
       advance(pq);
     }
-    Pos pc{(int)blockIdx.x, 0};
+    Pos pc = start(blockIdx.x);
     float yacc[ECOLS];
 #pragma unroll
     for (int j = 0; j < ECOLS; ++j) yacc[j] = 0.f;
@@ -382,13 +402,21 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
           ++dr;
         }
       }
-      if (pc.kb == a.nkb - 1) {
+      if (pc.kb == (SPLIT ? pc.khi : a.nkb) - 1) {
         // tile done: store this thread's 64 token columns of weight row n
         const int n = (pc.t / nch) * TC_ROWS + row;
         const int m0 = (pc.t % nch) * PF_TOK + ch * ECOLS;
-        if (ok && n < a.N) {
+        const int mlim = a.M - m0;
+        if constexpr (SPLIT) {
+          // partial tile [token][row]: for each token the warp's 32 rows are
+          // 128 contiguous bytes
+          float *slot = a.partial + ((size_t)(pc.t * KS + pc.sp) * PF_TOK + ch * ECOLS) * TC_ROWS + row;
+          if (ok) {
+#pragma unroll
+            for (int j = 0; j < ECOLS; ++j) slot[(size_t)j * TC_ROWS] = yacc[j];
+          }
+        } else if (ok && n < a.N) {
           float *yp = a.y + (size_t)m0 * a.N + n;
-          const int mlim = a.M - m0;
 #pragma unroll
           for (int j = 0; j < ECOLS; ++j) {
             if (j < mlim) *yp = I8 ? yacc[j] * __ldg(a.xs + m0 + j) : yacc[j];
@@ -408,6 +436,23 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
     tc::fence_after_sync();
     tc::dealloc(tmem, 512);
   }
+}
+
+// Split-K finish: Y[m, n] = sum over the KS splits, in split order, of the
+// partial tiles [item][token][row] (times the token scale for W4A8). One CTA
+// per (tile, token), one thread per weight row: reads and writes coalesced.
+__global__ void __launch_bounds__(TC_ROWS) tc_split_reduce_kernel(const float *__restrict__ partial,
+                                                                   const float *__restrict__ xs, float *y, int M,
+                                                                   int N, int nch, int ks) {
+  const int t = blockIdx.x, tok = blockIdx.y, r = threadIdx.x;
+  const int m = (t % nch) * PF_TOK + tok, n = (t / nch) * TC_ROWS + r;
+  pdl_wait_prior_grid();
+  pdl_launch_dependents();
+  if (m >= M || n >= N) return;
+  const float *p = partial + ((size_t)t * ks * PF_TOK + tok) * TC_ROWS + r;
+  float v = 0.f;
+  for (int sp = 0; sp < ks; ++sp) v += p[(size_t)sp * PF_TOK * TC_ROWS];
+  y[(size_t)m * N + n] = xs ? v * xs[m] : v;
 }
 
 }  // namespace lbc

@@ -60,10 +60,7 @@ def _rank_main(rank, world, port, m, n, k, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("m,n,k", [(1, 11008, 4096), (2, 301, 640)])
-def test_two_gpu_fused_allgather(m, n, k):
-    world = 2
+def _run(world, m, n, k):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -78,3 +75,15 @@ def test_two_gpu_fused_allgather(m, n, k):
         for kind, call, err in errs:
             assert kind != "exception", err
             assert err <= 1e-5, (rank, kind, call, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("m,n,k", [(1, 11008, 4096), (2, 301, 640)])
+def test_two_gpu_fused_allgather(m, n, k):
+    _run(2, m, n, k)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 3, reason="needs more than two GPUs")
+@pytest.mark.parametrize("m,n,k", [(1, 11008, 4096), (2, 1001, 384)])
+def test_all_gpus_fused_allgather(m, n, k):
+    _run(min(torch.cuda.device_count(), 8), m, n, k)

@@ -142,3 +142,23 @@ def test_prefill_w4a8_workspace(rng):
     assert L.lbc_gemm_w4a8_noalloc(xt.data_ptr(), 96, 1024, *args, y2.data_ptr(), P, st) == -1
     torch.cuda.synchronize()
     assert torch.equal(y0, y1)
+
+
+@pytest.mark.parametrize("fmt", ["w4a16", "w4a8", "mxfp4"])
+def test_prefill_without_split_k(rng, fmt):
+    """149 weight-row tiles fill the GPU: no split-K (plain stores); the other
+    prefill tests have few tiles and run split-K (adds into a zeroed Y)."""
+    x, w = _problem(rng, 128, 149 * 128, 256)
+    if fmt == "mxfp4":
+        W = lb.quantize_mxfp4(w)
+        R.assert_close(K.gemm_mxfp4(x, W), R.gemm_mxfp4_ref(x, W.qw, W.e8m0),
+                       R.abs_bound(x, R.dequant_mxfp4(W.qw, W.e8m0)), PF_TOL)
+        return
+    W = lb.quantize_int4(w, asym=True)
+    if fmt == "w4a16":
+        R.assert_close(K.gemm_w4a16(x, W), R.gemm_w4a16_ref(x, W.qw, W.scales, W.zeros),
+                       R.abs_bound(x, R.dequant_int4(W.qw, W.scales, W.zeros)), PF_TOL)
+    else:
+        xq, xs, asum = R.quant_act_int8_ref(x, W.kp)
+        R.assert_close(K.gemm_w4a8(x, W), R.gemm_w4a8_ref(xq, xs, asum, W.qw, W.scales, W.zeros),
+                       R.w4a8_bound(xq, xs, asum, W.qw, W.scales, W.zeros), W8_TOL)
