@@ -14,7 +14,7 @@
 namespace lbc {
 
 // one CTA per token row; a warp quantizes one 128-element group per step
-__global__ void quant_act_int8_kernel(const float *__restrict__ x, int Kp,
+__global__ void quant_act_int8_kernel(const float *x, int Kp,
                                       int8_t *__restrict__ xq, float *__restrict__ xs,
                                       int32_t *__restrict__ asum) {
   __shared__ float wmax[32];
@@ -28,7 +28,7 @@ __global__ void quant_act_int8_kernel(const float *__restrict__ x, int Kp,
 
   float amax = 0.0f;
   for (int k = tid * 4; k < Kp; k += blockDim.x * 4) {
-    const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + k));
+    const float4 v = ld_act(reinterpret_cast<const float4 *>(xr + k));
     amax = fmaxf(amax, fabsf(v.x));
     amax = fmaxf(amax, fabsf(v.y));
     amax = fmaxf(amax, fabsf(v.z));
@@ -52,7 +52,7 @@ __global__ void quant_act_int8_kernel(const float *__restrict__ x, int Kp,
   const int G = Kp >> 7;
   for (int g = warp; g < G; g += nw) {
     const int k = (g << 7) + lane * 4;
-    const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + k));
+    const float4 v = ld_act(reinterpret_cast<const float4 *>(xr + k));
     const float f[4] = {v.x, v.y, v.z, v.w};
     uint32_t packed = 0;
     int sum = 0;

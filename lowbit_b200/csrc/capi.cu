@@ -221,14 +221,18 @@ bool meta_aligned(int fmt, const lbc::GemvArgs &a) {
 // the int4 formats when no staged-kernel tiling was requested (mr, nr, kb,
 // order unset; nb = CTAs per SM is honoured).
 struct RowsPlan {
-  int mt = 1, ch = 1, r = 4, threads = 128, grid = 1, cps = 4;
+  int mt = 1, ch = 1, r = 4, threads = 128, grid = 1, cps = 4, passes = 1;
 };
 
 bool rows_eligible(int fmt, int M, int Kp, const lbc_params *p) {
-  // MXFP4's table decode is ALU-heavier; its staged kernel is faster at M = 1
-  if (M > 2 || fmt == lbc::FMT_MXFP4) return false;
   if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0)) return false;
   const int Cs = Kp / 32;
+  // W4A8 with 3-16 tokens: 4 or 8 tokens per pass (int8 activations in
+  // registers), one chunk per thread, so rows up to 8 warps x 32 chunks
+  if (M > 2) return fmt == lbc::FMT_W4A8 && M <= 16 && Cs <= lbc::ROWS_MAX_WARPS * 32;
+  // MXFP4's table decode is ALU-heavier: with two tokens its staged kernel is
+  // as fast or faster (measured), with one the decode kernel wins
+  if (fmt == lbc::FMT_MXFP4 && M > 1) return false;
   return Cs <= lbc::ROWS_MAX_WARPS * 32 * (M == 1 ? 4 : 2);
 }
 
@@ -256,9 +260,10 @@ int plan_rows(int fmt, int M, int N, int Kp, const lbc_params *p, RowsPlan &P) {
   const int nw = std::min(lbc::ROWS_MAX_WARPS, ceil_div(Cs, 32));
   int ch = ceil_div(Cs, nw * 32);
   if (ch == 3) ch = 4;
-  P.mt = M;
+  P.mt = M <= 2 ? M : (M <= 4 ? 4 : 8);
+  P.passes = ceil_div(M, P.mt);
   P.ch = ch;
-  P.r = (M == 1) ? (ch == 4 ? 2 : 4) : 2;
+  P.r = (M == 1) ? (ch == 4 ? 2 : 4) : (P.mt == 4 ? 4 : 2);
   P.threads = nw * 32;
   if (!lbc::rows_combo(P.mt, P.ch, P.r)) return fail(LBC_ERR_PARAMS, "decode tile not compiled");
   const int occ = rows_occupancy_cached(fmt, P.mt, P.ch, P.r, P.threads);
@@ -275,7 +280,7 @@ int run_rows(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
   RowsPlan P;
   if (int rc = plan_rows(fmt, a.M, a.N, a.Kp, p, P)) return rc;
   a.status = dev_info().status;
-  cudaError_t e = lbc::rows_launch(fmt, a, P.mt, P.ch, P.r, dim3(P.grid, 1, 1), P.threads, st);
+  cudaError_t e = lbc::rows_launch(fmt, a, P.mt, P.ch, P.r, dim3(P.grid, P.passes, 1), P.threads, st);
   if (e != cudaSuccess) return fail_cuda("decode gemv launch", e);
   return LBC_PATH_SIMT;
 }
@@ -330,8 +335,9 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *o
 
 // Kernel path: explicit requests are honoured; automatic selection sends one
 // or two tokens to the register-streamed decode kernel and three or more to
-// the tensor-core kernel (W4A8 from 32 tokens: below that its int32 dp4a SIMT
-// kernel is faster), except small matrices below 32 tokens: the tensor-core
+// the tensor-core kernel (W4A8 from 32 tokens, or 12 on large matrices: below
+// that its int32 dp4a SIMT kernel is faster), except small matrices below 32
+// tokens: the tensor-core
 // path's fixed cost (activation-block kernel, TMEM and pipeline set-up, about
 // 10-18 us on B200) exceeds the SIMT kernels' time there (measured: N*Kp below
 // 10M weights up to 4 tokens, below 6M up to 31).
@@ -340,7 +346,9 @@ bool want_tc(const lbc_params *p, int fmt, int M, int N, int Kp) {
   const bool automatic = !p || p->isa == LBC_PATH_AUTO || p->isa >= 2;
   if (!automatic) return false;
   if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
-  if (fmt == lbc::FMT_W4A8) return M >= 32;
+  // W4A8: the dp4a SIMT kernel up to 31 tokens, except large matrices
+  // (32M+ weights) from 12 tokens, where the tensor cores win (measured)
+  if (fmt == lbc::FMT_W4A8) return M >= 32 || (M >= 12 && (double)N * Kp >= 32e6);
   if (M < 3) return false;
   const double w = (double)N * Kp;
   if (M < 32 && w < (M <= 4 ? 10e6 : 6e6)) return false;
@@ -417,8 +425,8 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
     if (buf && buflen > 0)
       snprintf(buf, (size_t)buflen,
                "{\"path\": \"simt\", \"kernel\": \"rows\", \"mt\": %d, \"ch\": %d, \"r\": %d, "
-               "\"threads\": %d, \"grid\": %d, \"ctas_per_sm\": %d}",
-               R.mt, R.ch, R.r, R.threads, R.grid, R.cps);
+               "\"threads\": %d, \"grid\": %d, \"passes\": %d, \"ctas_per_sm\": %d}",
+               R.mt, R.ch, R.r, R.threads, R.grid, R.passes, R.cps);
     return LBC_PATH_SIMT;
   }
   GemvPlan P;

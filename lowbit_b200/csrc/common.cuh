@@ -32,6 +32,40 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
+// ---------------------------------------------------------------- activation loads
+// Kernels launched with programmatic dependent launch start while the kernel
+// before them in the stream (which produces their activations) is still
+// running, and read those activations only after griddepcontrol.wait. Such
+// data must not be read with ld.global.nc (__ldg): a non-coherent load
+// declares the data constant for the kernel's whole lifetime, so the compiler
+// may issue it before the wait and see the previous call's values. These
+// loads are coherent and volatile: never moved above the wait.
+__device__ __forceinline__ float ld_act(const float *p) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int ld_act(const int *p) {
+  int v;
+  asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_act(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_act(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int8_t ld_act(const int8_t *p) {
+  int16_t v;
+  asm volatile("ld.global.s8 %0, [%1];" : "=h"(v) : "l"(p));
+  return (int8_t)v;
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

@@ -393,14 +393,14 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
       if (FMT == FMT_W4A8) {
         uint4 vl = make_uint4(0, 0, 0, 0), vh = make_uint4(0, 0, 0, 0);
         if (ok) {
-          vl = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + lo));
-          vh = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + hi));
+          vl = ld_act(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + lo));
+          vh = ld_act(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + hi));
         }
         xl[i][t][0] = vl.x; xl[i][t][1] = vl.y; xl[i][t][2] = vl.z; xl[i][t][3] = vl.w;
         xh[i][t][0] = vh.x; xh[i][t][1] = vh.y; xh[i][t][2] = vh.z; xh[i][t][3] = vh.w;
         // z * asum[m,g] is subtracted once per group, in the group's first chunk,
         // exactly as the reference applies it (src/lowbit/csrc/kern_scalar.c:49-59)
-        xsum[i][t] = (ok && (kc & 3) == 0) ? __ldg(a.asum + (size_t)m * G + (kc >> 2)) : 0;
+        xsum[i][t] = (ok && (kc & 3) == 0) ? ld_act(a.asum + (size_t)m * G + (kc >> 2)) : 0;
       } else {
         const float4 *pl = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + lo);
         const float4 *ph = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.Kp + hi);
@@ -408,8 +408,8 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
         for (int q = 0; q < 4; ++q) {
           float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f), h4 = l4;
           if (ok) {
-            l4 = __ldg(pl + q);
-            h4 = __ldg(ph + q);
+            l4 = ld_act(pl + q);
+            h4 = ld_act(ph + q);
           }
           xr[i][t][4 * q + 0] = pack2(__float_as_uint(l4.x), __float_as_uint(h4.x));
           xr[i][t][4 * q + 1] = pack2(__float_as_uint(l4.y), __float_as_uint(h4.y));
@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(256, 1) gemv_kernel(const GemvArgs a) {
       const int m = m0 + t;
       if (r < rows && m < a.M) {
         float val = out_val;
-        if (FMT == FMT_W4A8) val *= __ldg(a.xs + m);
+        if (FMT == FMT_W4A8) val *= ld_act(a.xs + m);
         float *dst = a.y + (size_t)m * a.N + (r0 + r);
         if (a.atomic_out)
           atomicAdd(dst, val);

@@ -10,6 +10,9 @@ namespace {
 
 // (MT, CH, R) combinations: MT tokens per pass, CH chunks per thread, R rows per block
 #define LBC_ROWS_COMBOS(X) X(1, 1, 4) X(1, 2, 4) X(1, 4, 2) X(2, 1, 2) X(2, 2, 2)
+// W4A8 only: int8 activations are a quarter of fp32's registers, so 4 or 8
+// tokens per pass fit (one chunk per thread)
+#define LBC_ROWS_W8_COMBOS(X) X(4, 1, 4) X(8, 1, 2)
 
 template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false>
 cudaError_t rows_launch_nw(const GemvArgs &a, dim3 grid, cudaStream_t st) {
@@ -73,6 +76,9 @@ cudaError_t rows_launch_fmt(const GemvArgs &a, int mt, int ch, int r, dim3 grid,
 #define LBC_ROWS_L(MT, CH, R) \
   if (mt == MT && ch == CH && r == R) return rows_launch_one<FMT, MT, CH, R>(a, grid, threads, st);
   LBC_ROWS_COMBOS(LBC_ROWS_L)
+  if constexpr (FMT == FMT_W4A8) {
+    LBC_ROWS_W8_COMBOS(LBC_ROWS_L)
+  }
 #undef LBC_ROWS_L
   return cudaErrorInvalidConfiguration;
 }
@@ -91,6 +97,9 @@ int rows_occ_fmt(int mt, int ch, int r, int threads) {
 #define LBC_ROWS_O(MT, CH, R) \
   if (mt == MT && ch == CH && r == R) return rows_occ_one<FMT, MT, CH, R>(threads);
   LBC_ROWS_COMBOS(LBC_ROWS_O)
+  if constexpr (FMT == FMT_W4A8) {
+    LBC_ROWS_W8_COMBOS(LBC_ROWS_O)
+  }
 #undef LBC_ROWS_O
   return 0;
 }
@@ -105,6 +114,7 @@ bool rows_combo(int mt, int ch, int r) {
 #define LBC_ROWS_C(MT, CH, R) \
   if (mt == MT && ch == CH && r == R) return true;
   LBC_ROWS_COMBOS(LBC_ROWS_C)
+  LBC_ROWS_W8_COMBOS(LBC_ROWS_C)
 #undef LBC_ROWS_C
   return false;
 }

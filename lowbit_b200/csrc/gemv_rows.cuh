@@ -176,14 +176,14 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
       if (FMT == FMT_W4A8) {
         uint4 vl = make_uint4(0, 0, 0, 0), vh = make_uint4(0, 0, 0, 0);
         if (ok) {
-          vl = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + lo));
-          vh = __ldg(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + hi));
+          vl = ld_act(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + lo));
+          vh = ld_act(reinterpret_cast<const uint4 *>(a.xq + (size_t)m * a.Kp + hi));
         }
         xl[i][t][0] = vl.x; xl[i][t][1] = vl.y; xl[i][t][2] = vl.z; xl[i][t][3] = vl.w;
         xh[i][t][0] = vh.x; xh[i][t][1] = vh.y; xh[i][t][2] = vh.z; xh[i][t][3] = vh.w;
         // z * asum[m,g] is subtracted once per group, in its first chunk, as
         // the reference applies it (src/lowbit/csrc/kern_scalar.c:49-59)
-        xsum[i][t] = (ok && (c & 3) == 0) ? __ldg(a.asum + (size_t)m * G + (c >> 2)) : 0;
+        xsum[i][t] = (ok && (c & 3) == 0) ? ld_act(a.asum + (size_t)m * G + (c >> 2)) : 0;
       } else {
         const size_t xrow = (size_t)m * a.Kp * (XM == XM_GLU ? 2 : 1);
         const float4 *pl = reinterpret_cast<const float4 *>(a.x + xrow + lo);
@@ -192,12 +192,12 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
         for (int q = 0; q < 4; ++q) {
           float4 l4 = make_float4(0.f, 0.f, 0.f, 0.f), h4 = l4;
           if (ok) {
-            l4 = __ldg(pl + q);
-            h4 = __ldg(ph + q);
+            l4 = ld_act(pl + q);
+            h4 = ld_act(ph + q);
             if (XM == XM_RMSNORM) {
               if (a.xres) {
-                l4 = add4(l4, __ldg(reinterpret_cast<const float4 *>(a.xres + xrow + lo) + q));
-                h4 = add4(h4, __ldg(reinterpret_cast<const float4 *>(a.xres + xrow + hi) + q));
+                l4 = add4(l4, ld_act(reinterpret_cast<const float4 *>(a.xres + xrow + lo) + q));
+                h4 = add4(h4, ld_act(reinterpret_cast<const float4 *>(a.xres + xrow + hi) + q));
                 if (a.xout && blockIdx.x == 0) {
                   reinterpret_cast<float4 *>(a.xout + xrow + lo)[q] = l4;
                   reinterpret_cast<float4 *>(a.xout + xrow + hi)[q] = h4;
@@ -205,8 +205,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
               }
               ss[t] = sumsq4(h4, sumsq4(l4, ss[t]));
             } else if (XM == XM_GLU) {
-              l4 = glu4(l4, __ldg(pl + q + a.Kp / 4));
-              h4 = glu4(h4, __ldg(ph + q + a.Kp / 4));
+              l4 = glu4(l4, ld_act(pl + q + a.Kp / 4));
+              h4 = glu4(h4, ld_act(ph + q + a.Kp / 4));
             }
           }
           xr[i][t][4 * q + 0] = pack2(__float_as_uint(l4.x), __float_as_uint(h4.x));
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   }
   float xsc[MT];
 #pragma unroll
-  for (int t = 0; t < MT; ++t) xsc[t] = (FMT == FMT_W4A8 && m0 + t < a.M) ? __ldg(a.xs + m0 + t) : 1.f;
+  for (int t = 0; t < MT; ++t) xsc[t] = (FMT == FMT_W4A8 && m0 + t < a.M) ? ld_act(a.xs + m0 + t) : 1.f;
   const uint32_t MAG = opaque(0x4B000000u);
   uint32_t epoch = 0;
   float *const *ydst = nullptr;

@@ -526,7 +526,7 @@ __global__ void __maxnreg__(80) tcgemm_kernel(const __grid_constant__ CUtensorMa
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
       const int m = chunk * MT + t;
-      xsc[t] = (FMT == FMT_W4A8 && m < a.M) ? __ldg(a.xs + m) : 1.f;
+      xsc[t] = (FMT == FMT_W4A8 && m < a.M) ? ld_act(a.xs + m) : 1.f;
     }
     // per-(row, group) scale (and zero point for W4A8) of the two groups of a unit
     struct EMeta {
@@ -678,7 +678,7 @@ __global__ void __maxnreg__(80) tcgemm_kernel(const __grid_constant__ CUtensorMa
 #pragma unroll
             for (int t = 0; t < MT; ++t) {
               const int m = chunk * MT + t;
-              const int as = (m < a.M && gi < a.G) ? __ldg(a.asum + (size_t)m * a.G + gi) : 0;
+              const int as = (m < a.M && gi < a.G) ? ld_act(a.asum + (size_t)m * a.G + gi) : 0;
               yacc[t] = fmaf((float)(isum[t] - (int)mcur.z[h] * as), mcur.s[h], yacc[t]);
             }
           } else {
@@ -706,7 +706,7 @@ __global__ void __maxnreg__(80) tcgemm_kernel(const __grid_constant__ CUtensorMa
 // n = piece*MT + token, absent tokens / pieces / K positions zero. One CTA per
 // block; each thread writes whole 16-byte rows (8 bf16 or 16 int8 values).
 template <int FMT, int MT, int NPIECE, int KBLK = TC_KB>
-__global__ void __launch_bounds__(256) tc_bblock_kernel(const float *__restrict__ x, const int8_t *__restrict__ xq,
+__global__ void __launch_bounds__(256) tc_bblock_kernel(const float *x, const int8_t *xq,
                                                         uint8_t *__restrict__ out, int M, int Kp, int nkb,
                                                         int bbytes) {
   constexpr bool I8 = (FMT == FMT_W4A8);
@@ -730,9 +730,9 @@ __global__ void __launch_bounds__(256) tc_bblock_kernel(const float *__restrict_
         const int k = kb * KBLK + (kk >> 7) * 128 + tc_perm(FMT, kk & 127);
         if (k < Kp) {
           if (I8) {
-            w[e >> 2] |= (uint32_t)(uint8_t)xq[(size_t)m * Kp + k] << (8 * (e & 3));
+            w[e >> 2] |= (uint32_t)(uint8_t)ld_act(xq + (size_t)m * Kp + k) << (8 * (e & 3));
           } else {
-            float r = x[(size_t)m * Kp + k];
+            float r = ld_act(x + (size_t)m * Kp + k);
             uint16_t b = 0;
 #pragma unroll
             for (int p = 0; p < NPIECE; ++p) {

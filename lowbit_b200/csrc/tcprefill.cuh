@@ -419,7 +419,7 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
           float *yp = a.y + (size_t)m0 * a.N + n;
 #pragma unroll
           for (int j = 0; j < ECOLS; ++j) {
-            if (j < mlim) *yp = I8 ? yacc[j] * __ldg(a.xs + m0 + j) : yacc[j];
+            if (j < mlim) *yp = I8 ? yacc[j] * ld_act(a.xs + m0 + j) : yacc[j];
             yp += a.N;
           }
         }
@@ -441,8 +441,8 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
 // Split-K finish: Y[m, n] = sum over the KS splits, in split order, of the
 // partial tiles [item][token][row] (times the token scale for W4A8). One CTA
 // per (tile, token), one thread per weight row: reads and writes coalesced.
-__global__ void __launch_bounds__(TC_ROWS) tc_split_reduce_kernel(const float *__restrict__ partial,
-                                                                   const float *__restrict__ xs, float *y, int M,
+__global__ void __launch_bounds__(TC_ROWS) tc_split_reduce_kernel(const float *partial, const float *xs,
+                                                                   float *y, int M,
                                                                    int N, int nch, int ks) {
   const int t = blockIdx.x, tok = blockIdx.y, r = threadIdx.x;
   const int m = (t % nch) * PF_TOK + tok, n = (t / nch) * TC_ROWS + r;
@@ -451,8 +451,8 @@ __global__ void __launch_bounds__(TC_ROWS) tc_split_reduce_kernel(const float *_
   if (m >= M || n >= N) return;
   const float *p = partial + ((size_t)t * ks * PF_TOK + tok) * TC_ROWS + r;
   float v = 0.f;
-  for (int sp = 0; sp < ks; ++sp) v += p[(size_t)sp * PF_TOK * TC_ROWS];
-  y[(size_t)m * N + n] = xs ? v * xs[m] : v;
+  for (int sp = 0; sp < ks; ++sp) v += ld_act(p + (size_t)sp * PF_TOK * TC_ROWS);
+  y[(size_t)m * N + n] = xs ? v * ld_act(xs + m) : v;
 }
 
 }  // namespace lbc

@@ -33,6 +33,9 @@ def test_decode_plan_is_rows(m, k):
         assert plan["kernel"] == ("rows" if fits else "staged"), plan
         if fits:
             assert plan["mt"] == m, plan
+    # MXFP4 takes the decode kernel for one token only
+    plan = K.describe_plan("mxfp4", m, 300, kp)
+    assert plan["kernel"] == ("rows" if fits and m == 1 else "staged"), plan
 
 
 @pytest.mark.parametrize("m", [1, 2])
@@ -89,3 +92,41 @@ def test_decode_nan_scale_propagates(rng):
     W2 = lb.MXFP4Weights(W.qw, e, W.k)
     y = K.gemm_mxfp4(x, W2)
     assert np.isnan(y[0, 5]) and np.isfinite(np.delete(y[0], 5)).all()
+
+
+@pytest.mark.parametrize("m", [3, 4, 5, 8, 13, 16])
+@pytest.mark.parametrize("k", [96, 1000, 4096, 8192])
+@pytest.mark.parametrize("n", [1, 333])
+@pytest.mark.parametrize("asym", [False, True])
+def test_decode_w4a8_several_tokens(rng, m, k, n, asym):
+    """W4A8 with 3-16 tokens runs the decode kernel 4 or 8 tokens per pass
+    (rows of up to 8192 elements); results meet the W4A8 bound, exact int32
+    group sums included."""
+    x, w = _problem(rng, m, n, k)
+    W = lb.quantize_int4(w, asym=asym)
+    plan = K.describe_plan("w4a8", m, n, W.kp)
+    assert plan["kernel"] == "rows" and plan["mt"] == (4 if m <= 4 else 8), plan
+    a = lb.quantize_act_int8(x)
+    ref = R.gemm_w4a8_ref(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
+    bound = R.w4a8_bound(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
+    R.assert_close(K.gemm_w4a8(x, W), ref, bound, RTOL)
+    R.assert_close(K.gemm_w4a8_q(a, W), ref, bound, RTOL)
+
+
+@pytest.mark.parametrize("m", [5, 8, 16])
+def test_w4a8_fresh_activations_every_call(rng, m):
+    """The decode kernel starts while the activation quantizer before it is
+    still running and reads the quantized activations only after
+    griddepcontrol.wait; with a new X on every call, a read issued before the
+    wait would return the previous call's activations."""
+    import torch
+    w = rng.standard_normal((300, 4096)).astype(np.float32)
+    W = lb.quantize_int4(w)
+    Wd = W.cuda()
+    for _ in range(40):
+        x = rng.standard_normal((m, 4096)).astype(np.float32)
+        a = lb.quantize_act_int8(x)
+        ref = R.gemm_w4a8_ref(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
+        bound = R.w4a8_bound(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
+        y = K.gemm_w4a8(torch.from_numpy(x).cuda(), Wd).cpu().numpy()
+        R.assert_close(y, ref, bound, RTOL)
