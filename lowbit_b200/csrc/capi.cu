@@ -346,9 +346,15 @@ bool want_tc(const lbc_params *p, int fmt, int M, int N, int Kp) {
   const bool automatic = !p || p->isa == LBC_PATH_AUTO || p->isa >= 2;
   if (!automatic) return false;
   if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
-  // W4A8: the dp4a SIMT kernel up to 31 tokens, except large matrices
-  // (32M+ weights) from 12 tokens, where the tensor cores win (measured)
-  if (fmt == lbc::FMT_W4A8) return M >= 32 || (M >= 12 && (double)N * Kp >= 32e6);
+  // W4A8: the dp4a SIMT kernels up to 31 tokens (the decode kernel takes up
+  // to 16 tokens on rows of up to 8192), except large matrices (32M+
+  // weights) from 17 tokens, or from 12 when the rows are longer than the
+  // decode kernel takes, where the tensor cores win (measured)
+  if (fmt == lbc::FMT_W4A8) {
+    if (M >= 32) return true;
+    const bool big = (double)N * Kp >= 32e6;
+    return big && (M > 16 || (M >= 12 && Kp > lbc::ROWS_MAX_WARPS * 32 * 32));
+  }
   if (M < 3) return false;
   const double w = (double)N * Kp;
   if (M < 32 && w < (M <= 4 ? 10e6 : 6e6)) return false;

@@ -155,8 +155,9 @@ def effective_isa(kind: str, isa=None, m: int = 1, n: int | None = None, k: int 
     pid = _path_id(isa)
     if pid == -1:
         if kind == "w4a8":
-            big = n is not None and k is not None and n * pad_to(k, GROUP) >= 32e6
-            pid = 1 if m >= 32 or (m >= 12 and big) else 0
+            kp = pad_to(k, GROUP) if k is not None else 0
+            big = n is not None and k is not None and n * kp >= 32e6
+            pid = 1 if m >= 32 or (big and (m > 16 or (m >= 12 and kp > 8192))) else 0
         elif m < 3:
             pid = 0
         elif n is not None and k is not None and m < 32 and n * pad_to(k, GROUP) < (10e6 if m <= 4 else 6e6):
