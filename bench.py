@@ -546,6 +546,15 @@ def run_model(args) -> dict:
         m.generate_batch(prompts16, NEW, cache=c16, timings=t)
         runs16.append(t)
     clocks = clk.stop()
+    # one decode step of each batch inside an NVTX range, for profilers
+    # (ncu --nvtx --nvtx-include "model_decode_step_b1/" ...); untimed
+    for cache, rng_name in ((c1, "model_decode_step_b1"), (c16, "model_decode_step_b16")):
+        g, _ = m._decode_graph(cache)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push(rng_name)
+        g.replay()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
 
     def med(runs, key):
         return statistics.median(r[key] for r in runs)
@@ -567,7 +576,7 @@ def run_model(args) -> dict:
             "build_s": round(t_build, 1), "clocks": clocks}
     # parity and CPU baseline: the reference's computation on the host (its C
     # kernels for every linear), prefill then 3 teacher-forced decode steps
-    if ref_lib.available():
+    if ref_lib.available() and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         ocfg = O.Cfg(**{k: getattr(cfg, k) for k in O.Cfg.__dataclass_fields__})
         lin = {}
@@ -601,8 +610,9 @@ def run_model(args) -> dict:
                                           "lb_gemm_w4a16 for every linear (oracle/_ref) with the numpy glue, "
                                           "default tiles"}
     else:
-        line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference",
-                                "sample": "unavailable: oracle/_ref/liblowbit_ref.so not built"}
+        why = "skipped (--no-cpu-baseline)" if args.no_cpu_baseline else \
+            "unavailable: oracle/_ref/liblowbit_ref.so not built"
+        line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": why}
     return line
 
 

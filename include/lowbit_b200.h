@@ -233,8 +233,12 @@ int lbc_qkv_rope(const float *qkv, const float *bias, const float *cos_t, const 
                  int H, int KV, int D, int S_max, void *stream);
 /* causal grouped-query attention: query (i, h) attends to keys 0..pos + i % T
  * of KV head h / (H / KV); out [B*T, H*D] (src/lowbit/model.py:336-361).
- * D is 32, 64 or 128; at most 16 query heads per KV head; the scores of one
- * token's head group, G * S_max fp32, must fit in shared memory (227 KB). */
+ * D is 32, 64 or 128; at most 16 query heads per KV head. For caches longer
+ * than 1024 positions, when the (token, KV head) pairs fill at most half the
+ * SMs, keys are split in blocks of 64 over more CTAs and merged by a second
+ * kernel (scratch: one grow-only buffer per device and stream, which cannot
+ * first grow inside a stream capture); otherwise the scores of one token's
+ * head group, G * S_max fp32, must fit in shared memory (227 KB). */
 int lbc_attention(const float *q, const float *k_cache, const float *v_cache, const int32_t *pos,
                   float *out, int B, int T, int H, int KV, int D, int S_max, void *stream);
 /* W4A16 decode GEMMs with the operator before them fused into the kernel's

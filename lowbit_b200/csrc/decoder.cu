@@ -18,6 +18,9 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "../../include/lowbit_b200.h"
 #include "common.cuh"
@@ -245,6 +248,174 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, 
   }
 }
 
+// Key-split attention for few (token, KV head) pairs: CTA (i, kvh, sp) takes
+// keys [sp * ATT_SPLIT, min(L, (sp + 1) * ATT_SPLIT)) and writes, per query
+// head, its maximum score, the sum of exp(score - max) and the unnormalised
+// output sum_j exp(score_j - max) v_j; attention_combine_kernel merges the
+// splits in order. With FUSE_ROPE the split that holds position pos + t also
+// appends k and v there (no other split reads that key).
+constexpr int ATT_SPLIT = 64;
+constexpr int ATT_SPLIT_THREADS = 128;
+
+template <int D, bool FUSE_ROPE>
+__global__ void __launch_bounds__(ATT_SPLIT_THREADS) attention_split_kernel(
+    const float *q, const float *bias, const float *cos_t, const float *sin_t, float *k_cache, float *v_cache,
+    const int32_t *pos_p, float *ws, int T, int H, int KV, int S_max, int NS, float scale) {
+  __shared__ __align__(16) float qs[ATT_MAX_G * D];
+  __shared__ float sc[ATT_MAX_G][ATT_SPLIT];
+  __shared__ float part[ATT_SPLIT_THREADS / D][ATT_MAX_G][D];
+  const int G = H / KV;
+  const int i = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z, b = i / T, t = i % T;
+  const int p0 = *pos_p;
+  const int L = p0 + t + 1;
+  const int j0 = sp * ATT_SPLIT;
+  if (j0 >= L) return;  // split past the current length: nothing to do
+  const int nk = min(ATT_SPLIT, L - j0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int NWARP = ATT_SPLIT_THREADS / 32;
+  float *kb = k_cache + ((size_t)b * KV + kvh) * S_max * D;
+  float *vb = v_cache + ((size_t)b * KV + kvh) * S_max * D;
+  if (FUSE_ROPE) {
+    constexpr int half = D / 2;
+    const int W = (H + 2 * KV) * D;
+    const float *row = q + (size_t)i * W;
+    const int p = p0 + t;
+    const bool mine = p >= j0 && p < j0 + ATT_SPLIT;  // this split appends k and v
+    const float *cs = cos_t + (size_t)p * half, *sn = sin_t + (size_t)p * half;
+    for (int e = tid; e < (G + 1) * half; e += ATT_SPLIT_THREADS) {
+      const int hh = e / half, d = e % half;
+      if (hh == G && !mine) continue;
+      const int head = hh < G ? kvh * G + hh : H + kvh;
+      const int c1 = head * D + d, c2 = c1 + half;
+      float x1 = row[c1], x2 = row[c2];
+      if (bias) {
+        x1 = __fadd_rn(x1, bias[c1]);
+        x2 = __fadd_rn(x2, bias[c2]);
+      }
+      const float c = cs[d], sv = sn[d];
+      const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sv));
+      const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sv));
+      if (hh < G) {
+        qs[hh * D + d] = o1;
+        qs[hh * D + d + half] = o2;
+      } else {
+        kb[(size_t)p * D + d] = o1;
+        kb[(size_t)p * D + d + half] = o2;
+      }
+    }
+    if (mine) {
+      for (int d = tid; d < D; d += ATT_SPLIT_THREADS) {
+        const int c = (H + KV + kvh) * D + d;
+        float v = row[c];
+        if (bias) v = __fadd_rn(v, bias[c]);
+        vb[(size_t)p * D + d] = v;
+      }
+    }
+  } else {
+    const float *qb = q + ((size_t)i * H + (size_t)kvh * G) * D;
+    for (int e = tid; e < G * D; e += ATT_SPLIT_THREADS) qs[e] = qb[e];
+  }
+  __syncthreads();
+  if (tid < nk) {
+    const float4 *kr = reinterpret_cast<const float4 *>(kb + (size_t)(j0 + tid) * D);
+    float s[ATT_MAX_G];
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_G; ++h) s[h] = 0.f;
+#pragma unroll
+    for (int u0 = 0; u0 < D / 4; u0 += 8) {
+      float4 kv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) kv[u] = kr[u0 + u];
+#pragma unroll
+      for (int h = 0; h < ATT_MAX_G; ++h) {
+        if (h < G) {
+          const float4 *qh = reinterpret_cast<const float4 *>(qs + h * D) + u0;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float4 a = qh[u];
+            s[h] = __fmaf_rn(a.x, kv[u].x, s[h]);
+            s[h] = __fmaf_rn(a.y, kv[u].y, s[h]);
+            s[h] = __fmaf_rn(a.z, kv[u].z, s[h]);
+            s[h] = __fmaf_rn(a.w, kv[u].w, s[h]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_G; ++h)
+      if (h < G) sc[h][tid] = __fmul_rn(s[h], scale);
+  }
+  __syncthreads();
+  float *rec = ws + (((size_t)i * KV + kvh) * NS + sp) * (size_t)(G * (D + 2));  // [G][m, l, o[D]]
+  for (int h = warp; h < G; h += NWARP) {
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sc[h][j]);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int j = lane; j < nk; j += 32) {
+      const float e = expf(__fsub_rn(sc[h][j], mx));
+      sc[h][j] = e;
+      sum = __fadd_rn(sum, e);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      rec[h * (D + 2)] = mx;
+      rec[h * (D + 2) + 1] = sum;
+    }
+  }
+  __syncthreads();
+  constexpr int NG = ATT_SPLIT_THREADS / D;
+  const int d = tid % D, kg = tid / D;
+  float acc[ATT_MAX_G];
+#pragma unroll
+  for (int h = 0; h < ATT_MAX_G; ++h) acc[h] = 0.f;
+#pragma unroll 4
+  for (int j = kg; j < nk; j += NG) {
+    const float v = vb[(size_t)(j0 + j) * D + d];
+#pragma unroll
+    for (int h = 0; h < ATT_MAX_G; ++h)
+      if (h < G) acc[h] = __fmaf_rn(sc[h][j], v, acc[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < ATT_MAX_G; ++h)
+    if (h < G) part[kg][h][d] = acc[h];
+  __syncthreads();
+  for (int e = tid; e < G * D; e += ATT_SPLIT_THREADS) {
+    const int h = e / D, dd = e % D;
+    float o = 0.f;
+    for (int g = 0; g < NG; ++g) o = __fadd_rn(o, part[g][h][dd]);
+    rec[h * (D + 2) + 2 + dd] = o;
+  }
+}
+
+// out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M), M = max_s m_s, over the
+// splits that hold keys (s * ATT_SPLIT < L), in split order
+template <int D>
+__global__ void __launch_bounds__(256) attention_combine_kernel(const float *ws, const int32_t *pos_p, float *out,
+                                                                int T, int H, int KV, int NS) {
+  const int G = H / KV;
+  const int i = blockIdx.x, kvh = blockIdx.y, t = i % T;
+  const int L = *pos_p + t + 1;
+  const int ns = min(NS, (L + ATT_SPLIT - 1) / ATT_SPLIT);
+  const float *base = ws + ((size_t)i * KV + kvh) * NS * (size_t)(G * (D + 2));
+  const size_t stride = (size_t)G * (D + 2);
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int h = e / D, d = e % D;
+    float mx = -INFINITY;
+    for (int s = 0; s < ns; ++s) mx = fmaxf(mx, base[s * stride + h * (D + 2)]);
+    float den = 0.f, num = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float *r = base + s * stride + h * (D + 2);
+      const float w = expf(__fsub_rn(r[0], mx));
+      den = __fmaf_rn(r[1], w, den);
+      num = __fmaf_rn(r[2 + d], w, num);
+    }
+    out[((size_t)i * H + (size_t)kvh * G + h) * D + d] = __fdiv_rn(num, den);
+  }
+}
+
 __global__ void silu_mul_kernel(const float *gu, float *out, int I, size_t total) {
   for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (size_t)gridDim.x * blockDim.x) {
     const size_t r = e / I, c = e % I;
@@ -302,6 +473,30 @@ int lbc_qkv_rope(const float *qkv, const float *bias, const float *cos_t, const 
 
 namespace lbc {
 namespace {
+// Scratch of the key-split path, one grow-only buffer per (device, stream),
+// held until exit. It cannot grow inside a stream capture: a first call of
+// each shape outside the capture sizes it.
+float *att_workspace(size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  auto &slot = cache[{dev, st}];
+  if (slot.first && slot.second >= bytes) return static_cast<float *>(slot.first);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
+  if (slot.first) {
+    cudaStreamSynchronize(st);  // the previous buffer may still be in use on this stream
+    cudaFree(slot.first);
+    slot = {nullptr, 0};
+  }
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+  slot = {p, bytes};
+  return static_cast<float *>(p);
+}
+
 int attention_launch(const float *q, const float *bias, const float *cos_t, const float *sin_t, float *k_cache,
                      float *v_cache, const int32_t *pos, float *out, int B, int T, int H, int KV, int D, int S_max,
                      bool fuse, cudaStream_t st) {
@@ -309,13 +504,37 @@ int attention_launch(const float *q, const float *bias, const float *cos_t, cons
   if (D != 32 && D != 64 && D != 128) return shape_error("attention: head_dim must be 32, 64 or 128");
   const int G = H / KV;
   if (G > ATT_MAX_G) return shape_error("attention: more than 16 query heads per KV head");
-  const size_t smem = ((size_t)G * D * (1 + ATT_THREADS / D) + (size_t)G * S_max) * sizeof(float);
-  int dev = 0, optin = 0;
+  int dev = 0, optin = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  if (smem > (size_t)optin) return shape_error("attention: KV cache longer than shared memory allows");
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const dim3 grid(B * T, KV);
   const float scale = (float)(1.0 / std::sqrt((double)D));  // np.float32(1.0 / np.sqrt(D))
+  // long caches with few (token, KV head) pairs: split the keys over more
+  // CTAs (any cache length). Up to 1024 positions the single-pass kernel is
+  // as fast on B200 (measured in a whole decode step) and needs no scratch.
+  const int NS = (S_max + ATT_SPLIT - 1) / ATT_SPLIT;
+  if (2 * B * T * KV <= sms && NS > 16) {
+    const size_t bytes = (size_t)B * T * KV * NS * G * (D + 2) * sizeof(float);
+    float *ws = att_workspace(bytes, st);
+    if (!ws) return shape_error("attention: key-split scratch unavailable (allocation failed, or first use inside a stream capture)");
+    const dim3 gs(B * T, KV, NS);
+#define LBC_ATS(DD, F)                                                                                        \
+  {                                                                                                           \
+    attention_split_kernel<DD, F><<<gs, ATT_SPLIT_THREADS, 0, st>>>(q, bias, cos_t, sin_t, k_cache, v_cache, pos, \
+                                                                  ws, T, H, KV, S_max, NS, scale);            \
+    attention_combine_kernel<DD><<<grid, 256, 0, st>>>(ws, pos, out, T, H, KV, NS);                           \
+  }
+    if (fuse) {
+      if (D == 32) LBC_ATS(32, true) else if (D == 64) LBC_ATS(64, true) else LBC_ATS(128, true)
+    } else {
+      if (D == 32) LBC_ATS(32, false) else if (D == 64) LBC_ATS(64, false) else LBC_ATS(128, false)
+    }
+#undef LBC_ATS
+    return launch_status("attention (key split)");
+  }
+  const size_t smem = ((size_t)G * D * (1 + ATT_THREADS / D) + (size_t)G * S_max) * sizeof(float);
+  if (smem > (size_t)optin) return shape_error("attention: KV cache longer than shared memory allows");
 #define LBC_ATT(DD, F)                                                                                     \
   {                                                                                                        \
     auto k = attention_kernel<DD, F>;                                                                      \

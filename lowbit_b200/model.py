@@ -530,16 +530,21 @@ class Model:
             return live[1], live[2]
         B = cache.batch
         tok = torch.zeros(B, dtype=torch.int64, device="cuda")
-        s = torch.cuda.Stream()
+        # warm-up and capture on one persistent side stream: the library's
+        # per-(device, stream) scratch buffers are sized by the warm-up and
+        # cannot first grow inside the capture
+        if getattr(self, "_gstream", None) is None:
+            self._gstream = torch.cuda.Stream()
+        s = self._gstream
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):  # warm-up outside capture: workspaces, plans, cuBLAS handles
             saved = int(cache.pos.item())
             self._step(tok, cache)
             cache.pos.fill_(saved)
-        torch.cuda.current_stream().wait_stream(s)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with torch.cuda.graph(g, stream=s):
             self._step(tok, cache)
+        torch.cuda.current_stream().wait_stream(s)
         self._graphs = {"decode": (cache, g, tok)}  # one live decode graph per model
         return g, tok
 

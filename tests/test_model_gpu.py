@@ -228,3 +228,44 @@ def test_fused_decode_gemv_rejects_ineligible_calls():
     # x_out aliasing x
     assert L.lbc_gemm_w4a16_rmsnorm(x.data_ptr(), x.data_ptr(), x.data_ptr(), s.data_ptr(), 1e-6, 1, 256,
                                     q.data_ptr(), s.data_ptr(), None, 8, y.data_ptr(), P, None) == -1
+
+
+@pytest.mark.parametrize("B,S,pos", [(1, 1100, 0), (1, 1100, 130), (2, 4100, 4000), (3, 20000, 17000), (1, 300, 200)])
+def test_key_split_attention(B, S, pos):
+    """Long caches with few (sequence, KV head) pairs take the key-split path
+    (blocks of 64 keys merged by a second kernel; 20000 positions would not
+    fit the single-pass kernel's shared memory), short ones the single-pass
+    kernel: both equal a float64 softmax attention, and the fused RoPE variant
+    equals the separate kernels bit for bit."""
+    from lowbit_b200.kernels import lib
+    H, KV, D = 14, 2, 64
+    g = torch.Generator().manual_seed(B * 1000 + pos)
+    W = (H + 2 * KV) * D
+    qkv = torch.randn(B, W, generator=g).cuda()
+    bias = torch.randn(W, generator=g).cuda()
+    cos, sin = (torch.from_numpy(a).cuda() for a in PM.rope_tables(D, S, 1e6))
+    kc = torch.randn(B, KV, S, D, generator=g).cuda()
+    vc = torch.randn(B, KV, S, D, generator=g).cuda()
+    k2, v2 = kc.clone(), vc.clone()
+    p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    q = torch.empty(B, H * D, device="cuda")
+    o1, o2 = torch.empty(B, H * D, device="cuda"), torch.empty(B, H * D, device="cuda")
+    L, st = lib(), torch.cuda.current_stream().cuda_stream
+    assert L.lbc_qkv_rope(qkv.data_ptr(), bias.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(), q.data_ptr(),
+                          kc.data_ptr(), vc.data_ptr(), B, 1, H, KV, D, S, st) == 0
+    assert L.lbc_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), p.data_ptr(), o1.data_ptr(), B, 1, H, KV, D,
+                           S, st) == 0
+    assert L.lbc_rope_attention(qkv.data_ptr(), bias.data_ptr(), cos.data_ptr(), sin.data_ptr(), p.data_ptr(),
+                                k2.data_ptr(), v2.data_ptr(), o2.data_ptr(), B, H, KV, D, S, st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(kc, k2) and torch.equal(vc, v2)
+    assert torch.equal(o1, o2)
+    qd = q.double().view(B, H, D).cpu()
+    kd, vd = kc.double()[:, :, :pos + 1].cpu(), vc.double()[:, :, :pos + 1].cpu()
+    G = H // KV
+    ref = torch.empty(B, H, D, dtype=torch.float64)
+    for b in range(B):
+        for h in range(H):
+            s = (kd[b, h // G] @ qd[b, h]) / np.sqrt(D)
+            ref[b, h] = torch.softmax(s, 0) @ vd[b, h // G]
+    assert float((o1.double().cpu().view(B, H, D) - ref).abs().max()) < 1e-4
