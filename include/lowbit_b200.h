@@ -145,6 +145,26 @@ int lbc_gemm_w4a8_noalloc(const float *x, int M, int Kp, const uint8_t *qw,
                           const float *scales, const uint8_t *zeros, int N, float *y,
                           const lbc_params *p, void *stream);
 
+/* Host-buffer variants: x (M x Kp fp32) and y (M x N fp32) are HOST memory,
+ * as in the reference's own entry points lb_gemm_w4a16 / lb_gemm_mxfp4 /
+ * lb_gemm_w4a8 (src/lowbit/csrc/lowbit.h:104-112), while qw, scales, zeros
+ * and e8m0 are device memory (weights are uploaded once). Each call copies x
+ * to library-owned device staging (one per device and stream, grown on
+ * demand), runs the device entry point above on `stream`, copies y back and
+ * returns after the stream has drained, so y is ready on return. Pinned host
+ * buffers (cudaHostAlloc / cudaHostRegister) copy fastest; pageable ones
+ * work. Calls on one stream are serialised by the library. Not capturable
+ * (LBC_ERR_PARAMS while `stream` is capturing). */
+int lbc_gemm_w4a16_host(const float *x, int M, int Kp, const uint8_t *qw,
+                        const float *scales, const uint8_t *zeros, int N, float *y,
+                        const lbc_params *p, void *stream);
+int lbc_gemm_mxfp4_host(const float *x, int M, int Kp, const uint8_t *qw,
+                        const uint8_t *e8m0, int N, float *y, const lbc_params *p,
+                        void *stream);
+int lbc_gemm_w4a8_host(const float *x, int M, int Kp, const uint8_t *qw,
+                       const float *scales, const uint8_t *zeros, int N, float *y,
+                       const lbc_params *p, void *stream);
+
 /* W4A8 on pre-quantized activations: replaces lb_gemm_w4a8_q
  * (src/lowbit/csrc/lowbit.h:113-116, dispatch.c:259-268). */
 int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum,

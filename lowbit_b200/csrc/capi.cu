@@ -3,8 +3,11 @@
 // configuration. The reference's equivalents are the public functions of
 // src/lowbit/csrc/dispatch.c:205-305 and its tiling driver run() (:148-203).
 #include <algorithm>
+#include <array>
+#include <map>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 
@@ -694,6 +697,238 @@ int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw, c
   if (e == cudaErrorInvalidConfiguration) return fail(LBC_ERR_PARAMS, "decode tile has no fused all-gather variant");
   if (e != cudaSuccess) return fail_cuda("fused all-gather decode launch", e);
   return LBC_PATH_SIMT;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ host buffers
+
+namespace {
+
+// What a host-buffer call's captured work depends on besides the staging
+// addresses: format, shape, weight pointers and params.
+using HostKey = std::array<uint64_t, 8>;
+
+HostKey host_key(int fmt, int M, int N, int Kp, const void *w0, const void *w1, const void *w2,
+                 const lbc_params *p) {
+  HostKey k{};
+  k[0] = ((uint64_t)(uint32_t)fmt << 32) | (uint32_t)M;
+  k[1] = ((uint64_t)(uint32_t)N << 32) | (uint32_t)Kp;
+  k[2] = (uint64_t)(uintptr_t)w0;
+  k[3] = (uint64_t)(uintptr_t)w1;
+  k[4] = (uint64_t)(uintptr_t)w2;
+  if (p) {
+    k[5] = 1 | ((uint64_t)(uint32_t)p->isa << 32);
+    k[6] = ((uint64_t)(uint32_t)p->mr << 32) | (uint32_t)p->nr;
+    k[7] = ((uint64_t)(uint32_t)p->nb << 48) ^ ((uint64_t)(uint32_t)p->kb << 16) ^ (uint32_t)p->order ^
+           ((uint64_t)(uint32_t)p->nthreads << 40);
+  }
+  return k;
+}
+
+constexpr size_t HOST_GRAPHS_MAX = 64;
+
+// Per (device, stream) state of the host-buffer entry points: device staging
+// (X, Y, W4A8 workspace), pinned and mapped host bounce buffers for X and Y,
+// a private capture stream, and one instantiated CUDA graph per HostKey
+// holding [bounce -> X copy, the GEMM's launches, Y -> bounce copy]. The mutex is held
+// for a whole call, which ends with the stream drained, so the next call on
+// that stream can reuse every buffer.
+struct Stage {
+  std::mutex mu;
+  void *dev = nullptr;
+  size_t dev_bytes = 0;
+  void *hx = nullptr, *hy = nullptr;  // pinned, mapped: hx_d / hy_d are their device addresses
+  float *hx_d = nullptr, *hy_d = nullptr;
+  size_t hx_bytes = 0, hy_bytes = 0;
+  cudaStream_t cap = nullptr;
+  std::map<HostKey, std::pair<cudaGraphExec_t, int>> graphs;
+
+  void drop_graphs() {
+    for (auto &kv : graphs)
+      if (kv.second.first) cudaGraphExecDestroy(kv.second.first);
+    graphs.clear();
+  }
+};
+
+Stage *stage_of(cudaStream_t st) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, std::unique_ptr<Stage>> map;
+  int d = 0;
+  cudaGetDevice(&d);
+  const uint64_t key = ((uint64_t)(d & 63) << 58) ^ (uint64_t)(uintptr_t)st;
+  std::lock_guard<std::mutex> g(mu);
+  std::unique_ptr<Stage> &s = map[key];
+  if (!s) s.reset(new Stage);
+  return s.get();
+}
+
+inline size_t al256(size_t b) { return (b + 255) / 256 * 256; }
+
+// grow one staging buffer (device or pinned host) to at least `need` bytes
+int grow(Stage &s, void **buf, size_t *bytes, size_t need, bool host) {
+  if (*bytes >= need) return 0;
+  s.drop_graphs();  // captured graphs hold the old addresses
+  s.hx_d = s.hy_d = nullptr;
+  if (*buf) host ? cudaFreeHost(*buf) : cudaFree(*buf);
+  *buf = nullptr;
+  *bytes = 0;
+  const size_t nb = std::max(need, (size_t)1 << 16);
+  const cudaError_t e =
+      host ? cudaHostAlloc(buf, nb, cudaHostAllocPortable | cudaHostAllocMapped) : cudaMalloc(buf, nb);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *buf = nullptr;
+    return fail(LBC_ERR_ALLOC, host ? "cudaHostAlloc(host-call bounce buffer) failed"
+                                    : "cudaMalloc(host-call staging) failed");
+  }
+  *bytes = nb;
+  return 0;
+}
+
+// Copies and launches of one call, enqueued on `st`: X from the mapped
+// bounce buffer into device staging, the GEMM (launch(xd, yd, ws, st) enqueues
+// the device-pointer entry point), Y back into the mapped bounce buffer. The
+// copies are kernels (SM loads and stores of mapped host memory), which beat
+// copy-engine transfers at these sizes and overlap the GEMM's weight stream.
+template <class Launch>
+int enqueue_host(Stage &s, float *xd, float *yd, void *ws, size_t xb, size_t yb, cudaStream_t st,
+                 Launch &launch) {
+  const int sms = dev_info().sms;
+  cudaError_t e = lbc::launch_copy_f32(s.hx_d, xd, xb / sizeof(float), sms, st);
+  if (e != cudaSuccess) return fail_cuda("stage-in copy launch", e);
+  const int rc = launch(xd, yd, ws, st);
+  if (rc < 0) return rc;
+  e = lbc::launch_copy_f32(yd, s.hy_d, yb / sizeof(float), sms, st);
+  if (e != cudaSuccess) return fail_cuda("stage-out copy launch", e);
+  return rc;
+}
+
+// X is copied into the pinned bounce buffer, the call's graph (captured on
+// the first call with this key, after one uncaptured run on the private
+// stream that also serves that call) runs on `stream`, and Y is copied out
+// of the bounce buffer once the stream has drained.
+template <class Launch>
+int run_host(const HostKey &key, const float *x_host, int M, int Kp, int N, float *y_host, size_t ws_bytes,
+             void *stream, Launch launch) {
+  if (!x_host || !y_host) return fail(LBC_ERR_SHAPE, "NULL host pointer");
+  if (int rc = device_gate()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(st, &cs);
+  if (e != cudaSuccess) return fail_cuda("cudaStreamIsCapturing", e);
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(LBC_ERR_PARAMS, "host-buffer entry points synchronise their stream and cannot be captured");
+  const size_t xb = (size_t)M * Kp * sizeof(float), yb = (size_t)M * N * sizeof(float);
+  Stage &s = *stage_of(st);
+  std::lock_guard<std::mutex> g(s.mu);
+  if (!s.cap && (e = cudaStreamCreateWithFlags(&s.cap, cudaStreamNonBlocking)) != cudaSuccess) {
+    s.cap = nullptr;
+    return fail_cuda("cudaStreamCreateWithFlags", e);
+  }
+  if (int rc = grow(s, &s.dev, &s.dev_bytes, al256(xb) + al256(yb) + al256(ws_bytes), false)) return rc;
+  if (int rc = grow(s, &s.hx, &s.hx_bytes, xb, true)) return rc;
+  if (int rc = grow(s, &s.hy, &s.hy_bytes, yb, true)) return rc;
+  if (!s.hx_d || !s.hy_d) {
+    if ((e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&s.hx_d), s.hx, 0)) != cudaSuccess ||
+        (e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&s.hy_d), s.hy, 0)) != cudaSuccess) {
+      s.hx_d = s.hy_d = nullptr;
+      return fail_cuda("cudaHostGetDevicePointer", e);
+    }
+  }
+  uint8_t *base = static_cast<uint8_t *>(s.dev);
+  float *xd = reinterpret_cast<float *>(base);
+  float *yd = reinterpret_cast<float *>(base + al256(xb));
+  void *ws = ws_bytes ? base + al256(xb) + al256(yb) : nullptr;
+  memcpy(s.hx, x_host, xb);
+
+  auto it = s.graphs.find(key);
+  int rc;
+  if (it != s.graphs.end() && it->second.first) {
+    e = cudaGraphLaunch(it->second.first, st);
+    if (e != cudaSuccess) return fail_cuda("cudaGraphLaunch", e);
+    rc = it->second.second;
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
+  } else if (it != s.graphs.end()) {
+    // this key's work could not be captured: run it on `stream` directly
+    rc = enqueue_host(s, xd, yd, ws, xb, yb, st, launch);
+    e = cudaStreamSynchronize(st);
+    if (rc < 0) return rc;
+    if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
+  } else {
+    // first call with this key: drain `stream` (the call is ordered after its
+    // earlier work), run on the private stream, then capture the same work
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
+    rc = enqueue_host(s, xd, yd, ws, xb, yb, s.cap, launch);
+    e = cudaStreamSynchronize(s.cap);
+    if (rc < 0) return rc;
+    if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
+    if (s.graphs.size() >= HOST_GRAPHS_MAX) s.drop_graphs();
+    // a failed capture is not a failed call: the key runs uncaptured from now
+    // on, and lbc_last_error says why
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    e = cudaStreamBeginCapture(s.cap, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      const int crc = enqueue_host(s, xd, yd, ws, xb, yb, s.cap, launch);
+      e = cudaStreamEndCapture(s.cap, &graph);
+      if (crc < 0) {
+        char msg[400];
+        snprintf(msg, sizeof msg, "host-call graph capture failed: %s", g_err);
+        fail(crc, msg);
+      } else if (e != cudaSuccess || !graph) {
+        fail_cuda("host-call graph capture: cudaStreamEndCapture", e);
+      } else if ((e = cudaGraphInstantiate(&exec, graph, 0)) != cudaSuccess) {
+        fail_cuda("host-call graph capture: cudaGraphInstantiate", e);
+        exec = nullptr;
+      }
+      if (graph) cudaGraphDestroy(graph);
+    } else {
+      fail_cuda("host-call graph capture: cudaStreamBeginCapture", e);
+    }
+    cudaGetLastError();
+    s.graphs[key] = {exec, rc};
+  }
+  memcpy(y_host, s.hy, yb);
+  return rc;
+}
+
+}  // namespace
+
+// lbc_gemm_*_host: X and Y in host memory, as the reference's own entry points
+// take them (src/lowbit/csrc/dispatch.c:205-305), weights already on the
+// device. One call copies X in, runs the GEMM, copies Y out and returns after
+// the stream has drained.
+extern "C" {
+
+int lbc_gemm_w4a16_host(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
+                        const uint8_t *zeros, int N, float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  const HostKey key = host_key(lbc::FMT_W4A16, M, N, Kp, qw, scales, zeros, p);
+  return run_host(key, x, M, Kp, N, y, 0, stream, [&](const float *xd, float *yd, void *, cudaStream_t st) {
+    return lbc_gemm_w4a16(xd, M, Kp, qw, scales, zeros, N, yd, p, st);
+  });
+}
+
+int lbc_gemm_mxfp4_host(const float *x, int M, int Kp, const uint8_t *qw, const uint8_t *e8m0, int N,
+                        float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_MXBLOCK)) return rc;
+  const HostKey key = host_key(lbc::FMT_MXFP4, M, N, Kp, qw, e8m0, nullptr, p);
+  return run_host(key, x, M, Kp, N, y, 0, stream, [&](const float *xd, float *yd, void *, cudaStream_t st) {
+    return lbc_gemm_mxfp4(xd, M, Kp, qw, e8m0, N, yd, p, st);
+  });
+}
+
+int lbc_gemm_w4a8_host(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
+                       const uint8_t *zeros, int N, float *y, const lbc_params *p, void *stream) {
+  if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  const HostKey key = host_key(lbc::FMT_W4A8, M, N, Kp, qw, scales, zeros, p);
+  return run_host(key, x, M, Kp, N, y, w4a8_ws_layout(M, Kp, nullptr, nullptr), stream,
+                  [&](const float *xd, float *yd, void *ws, cudaStream_t st) {
+                    return lbc_gemm_w4a8(xd, M, Kp, qw, scales, zeros, N, yd, p, ws, st);
+                  });
 }
 
 }  // extern "C"

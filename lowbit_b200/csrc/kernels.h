@@ -15,6 +15,11 @@ cudaError_t launch_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, 
 
 cudaError_t launch_tc_selftest(int kind, int32_t *out, int *status, cudaStream_t st);
 
+// dst[0:n] = src[0:n] (floats, 16-byte aligned) by SM loads/stores, with
+// programmatic stream serialisation; either side may be mapped pinned host
+// memory (hostcopy.cu)
+cudaError_t launch_copy_f32(const float *src, float *dst, size_t n, int sms, cudaStream_t st);
+
 // one tensor-core GEMM call (tcgemm.cu)
 struct TcCall {
   int fmt;                 // FMT_W4A16 / FMT_MXFP4 / FMT_W4A8 (gemv.cuh ids: 0 / 1 / 2)

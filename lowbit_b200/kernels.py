@@ -86,6 +86,9 @@ def lib() -> C.CDLL:
         "lbc_gemm_mxfp4": ([_vp, _int, _int, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_gemm_w4a8_workspace_size": ([_int, _int], C.c_size_t),
         "lbc_gemm_w4a8": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp, _vp], _int),
+        "lbc_gemm_w4a16_host": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
+        "lbc_gemm_mxfp4_host": ([_vp, _int, _int, _vp, _vp, _int, _vp, _pp, _vp], _int),
+        "lbc_gemm_w4a8_host": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_gemm_w4a8_q": ([_vp, _vp, _vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
         "lbc_quant_act_int8": ([_vp, _int, _int, _vp, _vp, _vp, _vp], _int),
         "lbc_w4a8_group_acc": ([_vp, _vp, _int, _int, _vp, _vp, _int, _vp, _int, _vp], _int),
@@ -179,13 +182,23 @@ def auto_params(kind: str, m: int, n: int, k: int, isa=None, threads=None) -> Pa
     return _AUTO_MEMO[key]
 
 
+_P_AUTO = _Params(-1, 0, 0, 0, 0, 0, 0)
+
+
 def _params(p, isa, kind=None, shape=None) -> _Params:
+    if p is None and isa is None:
+        return _P_AUTO
     if isinstance(p, str):
         if p != "auto":
             raise ValueError(f"params must be a Params, None or 'auto', not {p!r}")
         p = auto_params(kind, *shape, isa=isa)
     p = p or Params()
     return _Params(_path_id(isa), p.mr, p.nr, p.nb, p.kb, p.order, 0)
+
+
+def _pref(params, isa, kind: str, m: int, n: int, k: int):
+    """byref(_Params) for a GEMM of m tokens on an n x k weight."""
+    return C.byref(_P_AUTO if params is None and isa is None else _params(params, isa, kind, (m, n, k)))
 
 
 def _check(rc: int, what: str) -> int:
@@ -220,7 +233,10 @@ class _Prepared:
         torch = _torch()
         from ._torch import to_cuda
         self.host = not isinstance(x, torch.Tensor)
-        if self.host:
+        if (not self.host and x.is_cuda and x.dtype == torch.float32 and x.dim() == 2
+                and x.shape[1] == kp and x.is_contiguous()):
+            xt = x          # already in the kernel's layout: no copies
+        elif self.host:
             x = np.asarray(x, np.float32)
             if x.ndim == 1:
                 x = x[None]
@@ -242,13 +258,46 @@ class _Prepared:
         return self.y.cpu().numpy() if self.host else self.y
 
 
+def _host_x(x, kp: int) -> np.ndarray:
+    """Host X as a C-contiguous float32 (M, kp) array, zero-padded to kp columns."""
+    a = np.asarray(x, np.float32)
+    if a.ndim == 1:
+        a = a[None]
+    if a.shape[1] != kp:
+        if a.shape[1] > kp:
+            raise ValueError(f"x has {a.shape[1]} columns, more than Kp={kp}")
+        a = np.pad(a, ((0, 0), (0, kp - a.shape[1])))
+    return np.ascontiguousarray(a)
+
+
+def _is_host(x) -> bool:
+    return not isinstance(x, _torch().Tensor)
+
+
+def _hptr(a: np.ndarray) -> int:
+    """Address of a C-contiguous host array's data."""
+    try:
+        return C.addressof(C.c_char.from_buffer(a))
+    except (TypeError, ValueError):   # read-only or zero-size buffers
+        return a.ctypes.data
+
+
 def _call(fn_name, *args):
     return getattr(lib(), fn_name)(*args)
 
 
+def _raw_stream(device_index: int) -> int:
+    """The current stream of a CUDA device as a raw handle (torch's own accessor)."""
+    return _torch()._C._cuda_getCurrentRawStream(device_index)
+
+
 def _stream():
-    from ._torch import stream_handle
-    return stream_handle()
+    torch = _torch()
+    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device())
+
+
+def _zp(d):
+    return None if d.zeros is None else d.zeros.data_ptr()
 
 
 # ---------------------------------------------------------------- GEMMs
@@ -256,23 +305,39 @@ def _stream():
 def gemm_w4a16(x, w: Int4Weights, params: Params | None = None, isa=None,
                threads: int | None = None, _prep: _Prepared | None = None):
     """Y = X @ dequant(W).T for int4 g128 weights (fp32 activations)."""
-    pr = _prep or _Prepared(x, w.kp, w.n)
     d = _dev_weights(w)
-    rc = _call("lbc_gemm_w4a16", pr.x.data_ptr(), pr.m, w.kp, d.qw.data_ptr(), d.scales.data_ptr(),
-               None if d.zeros is None else d.zeros.data_ptr(), w.n, pr.y.data_ptr(),
-               C.byref(_params(params, isa, "w4a16", (pr.m, w.n, w.k))), _stream())
-    _check(rc, "lbc_gemm_w4a16")
+    n, kp = w.n, w.kp
+    if _prep is None and _is_host(x):
+        xh = _host_x(x, kp)
+        m = xh.shape[0]
+        y = np.empty((m, n), np.float32)
+        _check(lib().lbc_gemm_w4a16_host(_hptr(xh), m, kp, d.qw.data_ptr(), d.scales.data_ptr(), _zp(d), n,
+                                          _hptr(y), _pref(params, isa, "w4a16", m, n, w.k), _stream()),
+               "lbc_gemm_w4a16")
+        return y
+    pr = _prep or _Prepared(x, kp, n)
+    _check(lib().lbc_gemm_w4a16(pr.x.data_ptr(), pr.m, kp, d.qw.data_ptr(), d.scales.data_ptr(), _zp(d), n,
+                                pr.y.data_ptr(), _pref(params, isa, "w4a16", pr.m, n, w.k),
+                                _raw_stream(pr.x.device.index)), "lbc_gemm_w4a16")
     return pr.result()
 
 
 def gemm_mxfp4(x, w: MXFP4Weights, params: Params | None = None, isa=None,
                threads: int | None = None, _prep: _Prepared | None = None):
     """Y = X @ dequant(W).T for OCP MXFP4 weights."""
-    pr = _prep or _Prepared(x, w.kp, w.n)
     d = _dev_weights(w)
-    rc = _call("lbc_gemm_mxfp4", pr.x.data_ptr(), pr.m, w.kp, d.qw.data_ptr(), d.e8m0.data_ptr(), w.n,
-               pr.y.data_ptr(), C.byref(_params(params, isa, "mxfp4", (pr.m, w.n, w.k))), _stream())
-    _check(rc, "lbc_gemm_mxfp4")
+    n, kp = w.n, w.kp
+    if _prep is None and _is_host(x):
+        xh = _host_x(x, kp)
+        m = xh.shape[0]
+        y = np.empty((m, n), np.float32)
+        _check(lib().lbc_gemm_mxfp4_host(_hptr(xh), m, kp, d.qw.data_ptr(), d.e8m0.data_ptr(), n, _hptr(y),
+                                          _pref(params, isa, "mxfp4", m, n, w.k), _stream()), "lbc_gemm_mxfp4")
+        return y
+    pr = _prep or _Prepared(x, kp, n)
+    _check(lib().lbc_gemm_mxfp4(pr.x.data_ptr(), pr.m, kp, d.qw.data_ptr(), d.e8m0.data_ptr(), n,
+                                pr.y.data_ptr(), _pref(params, isa, "mxfp4", pr.m, n, w.k),
+                                _raw_stream(pr.x.device.index)), "lbc_gemm_mxfp4")
     return pr.result()
 
 
@@ -293,13 +358,21 @@ def _workspace(nbytes: int):
 def gemm_w4a8(x, w: Int4Weights, params: Params | None = None, isa=None,
               threads: int | None = None, _prep: _Prepared | None = None):
     """fp32 X in; X is quantized per token to int8 inside the call (counted in timings)."""
-    pr = _prep or _Prepared(x, w.kp, w.n)
     d = _dev_weights(w)
-    ws = _workspace(int(lib().lbc_gemm_w4a8_workspace_size(pr.m, w.kp)))
-    rc = _call("lbc_gemm_w4a8", pr.x.data_ptr(), pr.m, w.kp, d.qw.data_ptr(), d.scales.data_ptr(),
-               None if d.zeros is None else d.zeros.data_ptr(), w.n, pr.y.data_ptr(),
-               C.byref(_params(params, isa, "w4a8", (pr.m, w.n, w.k))), ws.data_ptr(), _stream())
-    _check(rc, "lbc_gemm_w4a8")
+    n, kp = w.n, w.kp
+    if _prep is None and _is_host(x):
+        xh = _host_x(x, kp)
+        m = xh.shape[0]
+        y = np.empty((m, n), np.float32)
+        _check(lib().lbc_gemm_w4a8_host(_hptr(xh), m, kp, d.qw.data_ptr(), d.scales.data_ptr(), _zp(d), n,
+                                         _hptr(y), _pref(params, isa, "w4a8", m, n, w.k), _stream()),
+               "lbc_gemm_w4a8")
+        return y
+    pr = _prep or _Prepared(x, kp, n)
+    ws = _workspace(int(lib().lbc_gemm_w4a8_workspace_size(pr.m, kp)))
+    _check(lib().lbc_gemm_w4a8(pr.x.data_ptr(), pr.m, kp, d.qw.data_ptr(), d.scales.data_ptr(), _zp(d), n,
+                               pr.y.data_ptr(), _pref(params, isa, "w4a8", pr.m, n, w.k), ws.data_ptr(),
+                               _raw_stream(pr.x.device.index)), "lbc_gemm_w4a8")
     return pr.result()
 
 

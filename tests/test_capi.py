@@ -35,3 +35,15 @@ def test_version_query_needs_no_gpu():
 def test_kernels_are_built_for_sm100a_only():
     assert "arch=compute_100a,code=sm_100a" in " ".join(_build.ARCH)
     assert "--use_fast_math" not in _build.FLAGS
+
+
+def test_python_binding_declares_every_entry_point():
+    """lowbit_b200.kernels.lib() loads the library and sets a ctypes signature
+    for every entry point the header declares (no calls)."""
+    from lowbit_b200 import kernels as K
+    lib = K.lib()
+    for n in declared():
+        if n == "lbc_gemm_w4a8_noalloc":   # bound by its own test module
+            continue
+        fn = getattr(lib, n)
+        assert fn.argtypes is not None, f"{n} has no ctypes signature in lowbit_b200.kernels"
