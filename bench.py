@@ -528,6 +528,22 @@ def run_model(args) -> dict:
     t_build = time.perf_counter() - t_build
     V, P, NEW = cfg.vocab_size, 128, 128
     prompt = np.random.default_rng(0).integers(0, V, P)
+    # the packed-weight file: write the quantized model, read it back
+    # (no quantization), check the logits are the same
+    import tempfile
+    with tempfile.TemporaryDirectory() as td:
+        pk = Path(td) / "model.safetensors"
+        t0 = time.perf_counter()
+        PM.save_packed(m, pk)
+        t_save = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        m_pk = PM.load_packed(pk)
+        torch.cuda.synchronize()
+        t_load = time.perf_counter() - t0
+        packed = {"bytes": pk.stat().st_size, "save_s": round(t_save, 2), "load_s": round(t_load, 2),
+                  "logits_identical": bool(np.array_equal(m_pk.forward(prompt[:16], logits="all"),
+                                                          m.forward(prompt[:16], logits="all")))}
+        del m_pk
     prompts16 = np.random.default_rng(1).integers(0, V, (16, P))
     c1, c16 = m.new_cache(P + NEW), m.new_cache(P + NEW, batch=16)
     for _ in range(args.warmup):  # builds plans, workspaces and the decode graphs
@@ -575,7 +591,7 @@ def run_model(args) -> dict:
             "prefill_tok_s": round(P / med(runs1, "prefill_s"), 1),
             "batch16": {"decode_tok_s": round(dec16, 1), "prefill_tok_s": round(16 * P / med(runs16, "prefill_s"), 1),
                         "ms_per_step": round(1e3 * med(runs16, "decode_s") / (NEW - 1), 4)},
-            "build_s": round(t_build, 1), "clocks": clocks}
+            "build_s": round(t_build, 1), "packed_file": packed, "clocks": clocks}
     # parity and CPU baseline: the reference's computation on the host (its C
     # kernels for every linear), prefill then 3 teacher-forced decode steps
     if ref_lib.available() and not args.no_cpu_baseline:

@@ -25,6 +25,13 @@ def to_cuda(a, device=None) -> torch.Tensor:
         t = a if a.device == dev else a.to(dev)
         return t.contiguous()
     arr = np.ascontiguousarray(a)
+    if not arr.flags.writeable:
+        # a read-only view (a packed file's memory map): torch only reads it
+        # for the copy to the device
+        import warnings
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore", UserWarning)
+            return torch.from_numpy(arr).to(dev, non_blocking=False).contiguous()
     return torch.from_numpy(arr).to(dev, non_blocking=False).contiguous()
 
 

@@ -226,6 +226,23 @@ class _LowbitLinear(Linear):
         self.params = params
         self.nbytes = self.wq.nbytes
 
+    def _setup_packed(self, d, host, params):
+        """Packed weights read from a file: `d` on the GPU, `host` the same
+        arrays on the host (no quantization, no device-to-host copy)."""
+        self.d, self.wq, self.params = d, host, params
+        self.nbytes = host.nbytes
+
+    @classmethod
+    def from_packed(cls, host, b=None, threads=None, params=None, device=None):
+        """A linear on already packed weights (`host`: numpy arrays)."""
+        from ._torch import to_cuda
+        self = cls.__new__(cls)
+        self.n, self.k = host.n, host.k
+        self.b = None if b is None else to_cuda(np.asarray(b, np.float32), device)
+        self.threads = threads
+        self._setup_packed(host.cuda(device), host, params)
+        return self
+
     def _x(self, x):
         torch = _torch()
         if x.shape[1] != self.wq.kp:
@@ -378,7 +395,8 @@ class Model:
     """Decoder forward with quantized linears (src/lowbit/model.py:276-457)."""
 
     def __init__(self, cfg: ModelConfig, weights: dict, backend: str = "fp32", threads: int | None = None,
-                 asym: bool = False, quantize_lm_head: bool = True, params=None, int4_scale: str = "absmax"):
+                 asym: bool = False, quantize_lm_head: bool = True, params=None, int4_scale: str = "absmax",
+                 _packed: tuple | None = None):
         from ._torch import require_cuda, to_cuda
         require_cuda()
         if backend not in LINEARS:
@@ -392,22 +410,45 @@ class Model:
         def g(n):
             return np.asarray(W[n], np.float32)
 
+        def linear(name, cls, w, b):
+            """The linear `name`: quantized from fp32 (w(), b() give the
+            arrays), or built from a packed file's arrays (load_packed)."""
+            if _packed is None:
+                return cls(w(), b(), **kw)
+            return _packed_linear(name, cls, _packed, kw)
+
         self.embed = to_cuda(np.ascontiguousarray(g("model.embed_tokens.weight")))
         self.layers: list[Layer] = []
         for i in range(cfg.num_layers):
             p, a = f"model.layers.{i}.", f"model.layers.{i}.self_attn."
-            wqkv = np.concatenate([g(a + "q_proj.weight"), g(a + "k_proj.weight"), g(a + "v_proj.weight")], 0)
-            bqkv = (np.concatenate([g(a + "q_proj.bias"), g(a + "k_proj.bias"), g(a + "v_proj.bias")])
-                    if cfg.qkv_bias else None)
-            wgu = np.concatenate([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")], 0)
-            self.layers.append(Layer(ln1=to_cuda(g(p + "input_layernorm.weight")), qkv=lin(wqkv, bqkv, **kw),
-                                     o=lin(g(a + "o_proj.weight"), None, **kw),
-                                     ln2=to_cuda(g(p + "post_attention_layernorm.weight")),
-                                     gate_up=lin(wgu, None, **kw), down=lin(g(p + "mlp.down_proj.weight"), None, **kw)))
+
+            def wqkv(a=a):
+                return np.concatenate([g(a + "q_proj.weight"), g(a + "k_proj.weight"), g(a + "v_proj.weight")], 0)
+
+            def bqkv(a=a):
+                return (np.concatenate([g(a + "q_proj.bias"), g(a + "k_proj.bias"), g(a + "v_proj.bias")])
+                        if cfg.qkv_bias else None)
+
+            def wgu(p=p):
+                return np.concatenate([g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")], 0)
+
+            def none():
+                return None
+
+            self.layers.append(Layer(
+                ln1=to_cuda(g(p + "input_layernorm.weight")),
+                qkv=linear(p + "qkv", lin, wqkv, bqkv),
+                o=linear(p + "o", lin, lambda a=a: g(a + "o_proj.weight"), none),
+                ln2=to_cuda(g(p + "post_attention_layernorm.weight")),
+                gate_up=linear(p + "gate_up", lin, wgu, none),
+                down=linear(p + "down", lin, lambda p=p: g(p + "mlp.down_proj.weight"), none)))
         self.norm = to_cuda(g("model.norm.weight"))
-        head = g("model.embed_tokens.weight") if cfg.tie_word_embeddings or "lm_head.weight" not in W \
-            else g("lm_head.weight")
-        self.lm_head = (lin if quantize_lm_head else FP32Linear)(head, None, **kw)
+
+        def head():
+            return g("model.embed_tokens.weight") if cfg.tie_word_embeddings or "lm_head.weight" not in W \
+                else g("lm_head.weight")
+
+        self.lm_head = linear("lm_head", lin if quantize_lm_head else FP32Linear, head, lambda: None)
         cos, sin = rope_tables(cfg.head_dim, cfg.max_position, cfg.rope_theta)
         self.cos, self.sin = to_cuda(cos), to_cuda(sin)
         # decode steps fuse the norms and the SiLU*up into the w4a16 GEMVs
@@ -612,6 +653,70 @@ def rope_tables(head_dim: int, n_pos: int, theta: float) -> tuple[np.ndarray, np
     inv = 1.0 / theta ** (np.arange(0, head_dim, 2, dtype=np.float64) / head_dim)
     ang = np.arange(n_pos, dtype=np.float64)[:, None] * inv[None]
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+# ---------------------------------------------------------------- packed files
+
+PACKED_VERSION = "1"
+
+
+def _packed_linear(name: str, cls, packed: tuple, kw: dict):
+    """Linear `name` of a packed file: its packed container (or, for an fp32
+    linear, `<name>.weight`) and optional `<name>.bias`."""
+    weights, extra = packed
+    b = extra.get(name + ".bias")
+    if cls is FP32Linear:
+        if name + ".weight" not in extra:
+            raise ValueError(f"{name}: the file holds no fp32 weight for an fp32 linear")
+        return FP32Linear(extra[name + ".weight"], b, **kw)
+    if name not in weights:
+        raise ValueError(f"{name}: the file holds no packed weights")
+    host = weights[name]
+    from .formats import Int4Weights, MXFP4Weights
+    want = MXFP4Weights if cls is MXFP4Linear else Int4Weights
+    if not isinstance(host, want):
+        raise ValueError(f"{name}: packed as {type(host).__name__}, backend {cls.kind} needs {want.__name__}")
+    return cls.from_packed(host, b, kw.get("threads"), kw.get("params"))
+
+
+def save_packed(model: Model, path: Path | str) -> None:
+    """Write `model` as a packed-weight file (lowbit_b200.packed): every
+    quantized linear's packed arrays as consumed by the kernels, fp32 linears,
+    biases, norms and the embedding, and the configuration in the metadata,
+    so that load_packed rebuilds the same model without quantizing."""
+    from dataclasses import asdict
+
+    from . import packed as PK
+    weights, extra = {}, {"model.embed_tokens.weight": model.embed, "model.norm.weight": model.norm}
+    named = [("lm_head", model.lm_head)]
+    for i, L in enumerate(model.layers):
+        p = f"model.layers.{i}."
+        extra[p + "input_layernorm.weight"] = L.ln1
+        extra[p + "post_attention_layernorm.weight"] = L.ln2
+        named += [(p + "qkv", L.qkv), (p + "o", L.o), (p + "gate_up", L.gate_up), (p + "down", L.down)]
+    for name, lin in named:
+        if isinstance(lin, FP32Linear):
+            extra[name + ".weight"] = lin.w
+        else:
+            weights[name] = lin.wq
+        if lin.b is not None:
+            extra[name + ".bias"] = lin.b
+    meta = {"lowbit_b200.packed": PACKED_VERSION, "config": json.dumps(asdict(model.cfg)),
+            "backend": model.backend, "asym": int(model.asym), "quantize_lm_head": int(model.quantize_lm_head),
+            "int4_scale": model.int4_scale}
+    PK.save_weights(path, weights, extra, meta)
+
+
+def load_packed(path: Path | str, threads: int | None = None, params=None) -> Model:
+    """A model written by save_packed, with its weights uploaded as stored."""
+    from . import packed as PK
+    weights, extra, meta = PK.load_weights(path)
+    if meta.get("lowbit_b200.packed") != PACKED_VERSION:
+        raise ValueError(f"{path}: not a lowbit_b200 packed model (version {meta.get('lowbit_b200.packed')!r})")
+    cfg = ModelConfig(**json.loads(meta["config"]))
+    return Model(cfg, extra, backend=meta["backend"], threads=threads, asym=bool(int(meta["asym"])),
+                 quantize_lm_head=bool(int(meta["quantize_lm_head"])), params=params,
+                 int4_scale=meta["int4_scale"], _packed=(weights, extra))
 
 
 # ---------------------------------------------------------------- loading
