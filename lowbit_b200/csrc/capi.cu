@@ -260,9 +260,18 @@ int rows_occupancy_cached(int fmt, int mt, int ch, int r, int threads) {
 int plan_rows(int fmt, int M, int N, int Kp, const lbc_params *p, RowsPlan &P) {
   const DevInfo di = dev_info();
   const int Cs = Kp / 32;
-  const int nw = std::min(lbc::ROWS_MAX_WARPS, ceil_div(Cs, 32));
-  int ch = ceil_div(Cs, nw * 32);
-  if (ch == 3) ch = 4;
+  // one chunk per thread while a team of up to 8 warps (16 for one or two
+  // tokens, except one W4A8 token, whose lighter two-chunk tile measured
+  // faster) covers the row; longer rows take 2 or 4 chunks per thread with
+  // the fewest warps that still cover the row (threads past the row's end
+  // would decode a clamped chunk against zero activations: wasted issue)
+  const bool wide = M == 2 || (M == 1 && fmt != lbc::FMT_W4A8);
+  int ch = 1, nw = ceil_div(Cs, 32);
+  if (nw > (wide ? lbc::ROWS_WIDE_WARPS : lbc::ROWS_MAX_WARPS)) {
+    ch = ceil_div(Cs, lbc::ROWS_MAX_WARPS * 32);
+    if (ch == 3) ch = 4;
+    nw = std::min(lbc::ROWS_MAX_WARPS, ceil_div(Cs, 32 * ch));
+  }
   P.mt = M <= 2 ? M : (M <= 4 ? 4 : 8);
   P.passes = ceil_div(M, P.mt);
   P.ch = ch;

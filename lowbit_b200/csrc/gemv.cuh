@@ -32,8 +32,12 @@ namespace lbc {
 
 enum : int { FMT_W4A16 = 0, FMT_MXFP4 = 1, FMT_W4A8 = 2 };
 
-// largest row team of the register-streamed decode kernel (gemv_rows.cuh)
+// largest row team of the register-streamed decode kernel (gemv_rows.cuh);
+// teams of one chunk per thread and one or two tokens may be up to
+// ROWS_WIDE_WARPS warps (one CTA per SM at <= 128 registers), which covers
+// rows of up to 16384 elements without the register-heavy multi-chunk tiles
 constexpr int ROWS_MAX_WARPS = 8;
+constexpr int ROWS_WIDE_WARPS = 16;
 
 struct GemvArgs {
   const float *x;       // [M, Kp] fp32 (W4A16 / MXFP4)

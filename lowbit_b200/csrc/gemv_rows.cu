@@ -29,9 +29,23 @@ cudaError_t rows_launch_nw(const GemvArgs &a, dim3 grid, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, gemv_rows_kernel<FMT, MT, CH, R, NW, GATHER>, a);
 }
 
-// the row team is 1..ROWS_MAX_WARPS (8) warps
+// the row team is 1..ROWS_MAX_WARPS (8) warps, or up to ROWS_WIDE_WARPS (16)
+// with one chunk per thread and one or two tokens
 template <int FMT, int MT, int CH, int R, bool GATHER = false>
 cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStream_t st) {
+  if constexpr (CH == 1 && MT <= 2) {
+    switch (threads / 32) {
+      case 9: return rows_launch_nw<FMT, MT, CH, R, 9, GATHER>(a, grid, st);
+      case 10: return rows_launch_nw<FMT, MT, CH, R, 10, GATHER>(a, grid, st);
+      case 11: return rows_launch_nw<FMT, MT, CH, R, 11, GATHER>(a, grid, st);
+      case 12: return rows_launch_nw<FMT, MT, CH, R, 12, GATHER>(a, grid, st);
+      case 13: return rows_launch_nw<FMT, MT, CH, R, 13, GATHER>(a, grid, st);
+      case 14: return rows_launch_nw<FMT, MT, CH, R, 14, GATHER>(a, grid, st);
+      case 15: return rows_launch_nw<FMT, MT, CH, R, 15, GATHER>(a, grid, st);
+      case 16: return rows_launch_nw<FMT, MT, CH, R, 16, GATHER>(a, grid, st);
+      default: break;
+    }
+  }
   switch (threads / 32) {
     case 1: return rows_launch_nw<FMT, MT, CH, R, 1, GATHER>(a, grid, st);
     case 2: return rows_launch_nw<FMT, MT, CH, R, 2, GATHER>(a, grid, st);
@@ -58,6 +72,19 @@ int rows_occ_nw() {
 
 template <int FMT, int MT, int CH, int R>
 int rows_occ_one(int threads) {
+  if constexpr (CH == 1 && MT <= 2) {
+    switch (threads / 32) {
+      case 9: return rows_occ_nw<FMT, MT, CH, R, 9>();
+      case 10: return rows_occ_nw<FMT, MT, CH, R, 10>();
+      case 11: return rows_occ_nw<FMT, MT, CH, R, 11>();
+      case 12: return rows_occ_nw<FMT, MT, CH, R, 12>();
+      case 13: return rows_occ_nw<FMT, MT, CH, R, 13>();
+      case 14: return rows_occ_nw<FMT, MT, CH, R, 14>();
+      case 15: return rows_occ_nw<FMT, MT, CH, R, 15>();
+      case 16: return rows_occ_nw<FMT, MT, CH, R, 16>();
+      default: break;
+    }
+  }
   switch (threads / 32) {
     case 1: return rows_occ_nw<FMT, MT, CH, R, 1>();
     case 2: return rows_occ_nw<FMT, MT, CH, R, 2>();

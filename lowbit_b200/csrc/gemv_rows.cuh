@@ -79,7 +79,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   static_assert(XM == XM_PLAIN || FMT == FMT_W4A16, "fused prologues are W4A16 only");
   constexpr int V = R * MT;
   static_assert(V <= 32 && (V & (V - 1)) == 0, "R*MT must be a power of two <= 32");
-  static_assert(NW >= 1 && NW <= ROWS_MAX_WARPS, "1..ROWS_MAX_WARPS warps per row team");
+  static_assert(NW >= 1 && (NW <= ROWS_MAX_WARPS || (NW <= ROWS_WIDE_WARPS && CH == 1 && MT <= 2)),
+                "1..ROWS_MAX_WARPS warps per row team (ROWS_WIDE_WARPS with one chunk and token pair)");
   constexpr int NT = NW * 32;
   __shared__ float red[2][NW][V];
 

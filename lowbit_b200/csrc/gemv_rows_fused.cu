@@ -26,6 +26,19 @@ cudaError_t fused_nw(const GemvArgs &a, dim3 grid, cudaStream_t st) {
 
 template <int XM, int MT, int CH, int R>
 cudaError_t fused_one(const GemvArgs &a, dim3 grid, int threads, cudaStream_t st) {
+  if constexpr (CH == 1 && MT <= 2) {
+    switch (threads / 32) {
+      case 9: return fused_nw<XM, MT, CH, R, 9>(a, grid, st);
+      case 10: return fused_nw<XM, MT, CH, R, 10>(a, grid, st);
+      case 11: return fused_nw<XM, MT, CH, R, 11>(a, grid, st);
+      case 12: return fused_nw<XM, MT, CH, R, 12>(a, grid, st);
+      case 13: return fused_nw<XM, MT, CH, R, 13>(a, grid, st);
+      case 14: return fused_nw<XM, MT, CH, R, 14>(a, grid, st);
+      case 15: return fused_nw<XM, MT, CH, R, 15>(a, grid, st);
+      case 16: return fused_nw<XM, MT, CH, R, 16>(a, grid, st);
+      default: break;
+    }
+  }
   switch (threads / 32) {
     case 1: return fused_nw<XM, MT, CH, R, 1>(a, grid, st);
     case 2: return fused_nw<XM, MT, CH, R, 2>(a, grid, st);
