@@ -345,6 +345,97 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *o
   return xq_bytes + xs_bytes + as_bytes + tc_bytes;
 }
 
+// ------------------------------------------------------------------ few-token path
+// Partial sums of the few-token kernel's K ranges: one grow-only buffer per
+// (device, stream), so a decode loop issues no allocation; while the stream
+// is being captured a growth is a stream-ordered allocation freed after the
+// launches
+struct TokScratch {
+  float *p;
+  bool owned;
+};
+TokScratch tok_scratch(size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, std::pair<void *, size_t>> cache;
+  int d = 0;
+  cudaGetDevice(&d);
+  const uint64_t key = ((uint64_t)(d & 63) << 58) ^ (uint64_t)(uintptr_t)st;
+  std::lock_guard<std::mutex> g(mu);
+  auto &slot = cache[key];
+  if (slot.first && slot.second >= bytes) return {static_cast<float *>(slot.first), false};
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  void *p = nullptr;
+  if (cs != cudaStreamCaptureStatusNone) {
+    if (cudaMallocAsync(&p, bytes, st) != cudaSuccess) {
+      cudaGetLastError();
+      return {nullptr, false};
+    }
+    return {static_cast<float *>(p), true};
+  }
+  if (slot.first) {
+    cudaStreamSynchronize(st);
+    cudaFree(slot.first);
+    slot = {nullptr, 0};
+  }
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return {nullptr, false};
+  }
+  slot = {p, bytes};
+  return {static_cast<float *>(p), false};
+}
+
+struct TokPlan {
+  int r, warps, ks;
+};
+
+// rows per lane (2 once that still gives a CTA per SM); K ranges only for
+// rows of 2048+ elements (the second kernel that adds the ranges costs more
+// than it saves on short rows): about two CTAs per SM, two units per range
+// at least, each range's activations within shared memory; warps per CTA
+// (two K steps each at least)
+TokPlan tok_plan(int fmt, int M, int N, int Kp) {
+  const DevInfo di = dev_info();
+  const int spu = fmt == lbc::FMT_MXFP4 ? 1 : 4;  // K steps per unit (group / block)
+  const int U = Kp / 32 / spu;
+  TokPlan P;
+  P.r = ceil_div(N, 64) >= di.sms ? 2 : 1;
+  const int ctas = ceil_div(N, 32 * P.r) * ceil_div(M, 8);
+  int ks = Kp >= 2048 ? std::max(1, std::min(U / 2, 2 * di.sms / ctas)) : 1;
+  const int maxkp = lbc::tok_max_kp(di.smem_optin);
+  while (ks < U && 32 * spu * ceil_div(U, ks) > maxkp) ++ks;
+  P.ks = ks;
+  P.warps = std::max(1, std::min(16, spu * ceil_div(U, ks) / 2));
+  return P;
+}
+
+// The few-token kernel serves W4A16 with 8-16 tokens and MXFP4 with 4-16 on
+// automatic paths for matrices of up to LBC_TOK_MAX_WEIGHTS weights, where it
+// beats both the staged SIMT kernel and the tensor-core path's fixed cost
+// (measured: e.g. 896x896 at 16 tokens 14.4 -> 5.4 us, 896x4864 29 -> 13 us)
+constexpr double LBC_TOK_MAX_WEIGHTS = 5e6;
+bool want_tok(const lbc_params *p, int fmt, int M, int N, int Kp) {
+  if (fmt == lbc::FMT_W4A8) return false;
+  if (p && (p->isa != LBC_PATH_AUTO && p->isa < 2)) return false;
+  if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
+  if (M > 16 || M < (fmt == lbc::FMT_MXFP4 ? 4 : 8)) return false;
+  return (double)N * Kp <= LBC_TOK_MAX_WEIGHTS;
+}
+
+int run_tok(int fmt, const lbc::GemvArgs &a, cudaStream_t st) {
+  const TokPlan P = tok_plan(fmt, a.M, a.N, a.Kp);
+  TokScratch sc{nullptr, false};
+  if (P.ks > 1) {
+    sc = tok_scratch(sizeof(float) * (size_t)P.ks * a.M * a.N, st);
+    if (!sc.p) return fail(LBC_ERR_ALLOC, "few-token GEMM partial-sum buffer allocation failed");
+  }
+  cudaError_t e = lbc::tok_gemm(fmt, a, P.r, P.warps, P.ks, sc.p, st);
+  if (sc.owned) cudaFreeAsync(sc.p, st);
+  if (e != cudaSuccess) return fail_cuda("few-token GEMM launch", e);
+  return LBC_PATH_SIMT;
+}
+
 // Kernel path: explicit requests are honoured; automatic selection sends one
 // or two tokens to the register-streamed decode kernel and three or more to
 // the tensor-core kernel (W4A8 from 32 tokens, or 12 on large matrices: below
@@ -431,6 +522,14 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
   if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
   if (int rc = device_gate()) return rc;
   const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
+  if (want_tok(p, fmt, M, N, Kp)) {
+    const TokPlan P = tok_plan(fmt, M, N, Kp);
+    if (buf && buflen > 0)
+      snprintf(buf, (size_t)buflen,
+               "{\"path\": \"simt\", \"kernel\": \"tok\", \"passes\": %d, \"r\": %d, \"warps\": %d, \"ksplit\": %d}",
+               ceil_div(M, 8), P.r, P.warps, P.ks);
+    return LBC_PATH_SIMT;
+  }
   if (want_tc(p, fmt, M, N, Kp)) {
     if (buf && buflen > 0)
       snprintf(buf, (size_t)buflen, "{\"path\": \"tcgen05\", \"kernel\": \"%s\"}",
@@ -466,6 +565,12 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_tok(p, lbc::FMT_W4A16, M, N, Kp)) {
+    lbc::GemvArgs a{};
+    a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+    a.M = M; a.N = N; a.Kp = Kp;
+    return run_tok(lbc::FMT_W4A16, a, static_cast<cudaStream_t>(stream));
+  }
   if (want_tc(p, lbc::FMT_W4A16, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A16; c.x = x; c.qw = qw; c.scales = scales; c.zeros = zeros; c.y = y;
@@ -525,6 +630,12 @@ int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8
   if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_tok(p, lbc::FMT_MXFP4, M, N, Kp)) {
+    lbc::GemvArgs a{};
+    a.x = x; a.qw = qw; a.e8m0 = e8m0; a.y = y;
+    a.M = M; a.N = N; a.Kp = Kp;
+    return run_tok(lbc::FMT_MXFP4, a, static_cast<cudaStream_t>(stream));
+  }
   if (want_tc(p, lbc::FMT_MXFP4, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_MXFP4; c.x = x; c.qw = qw; c.e8m0 = e8m0; c.y = y;

@@ -15,6 +15,16 @@ cudaError_t launch_w4a8_group_acc(const int8_t *xq, const int32_t *asum, int M, 
 
 cudaError_t launch_tc_selftest(int kind, int32_t *out, int *status, cudaStream_t st);
 
+struct GemvArgs;  // gemv.cuh
+
+// few-token SIMT GEMM (gemv_tok.cu), W4A16 / MXFP4, 1 <= M <= 16, Kp <=
+// tok_max_kp(opt-in shared memory per block) for ks == 1: `r` (1 or 2) rows
+// per lane, `warps` (<= 16) warps per CTA, K split into `ks` ranges whose
+// partial sums go to `part` (ks * M * N floats) and are added by a second
+// kernel
+int tok_max_kp(int smem_optin);
+cudaError_t tok_gemm(int fmt, const GemvArgs &g, int r, int warps, int ks, float *part, cudaStream_t st);
+
 // dst[0:n] = src[0:n] (floats, 16-byte aligned) by SM loads/stores, with
 // programmatic stream serialisation; either side may be mapped pinned host
 // memory (hostcopy.cu)

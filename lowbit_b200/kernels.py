@@ -30,7 +30,7 @@ from functools import lru_cache
 import numpy as np
 
 from ._build import build
-from .formats import GROUP, Int4Weights, Int8Acts, MXFP4Weights, pad_to
+from .formats import GROUP, MXBLOCK, Int4Weights, Int8Acts, MXFP4Weights, pad_to
 
 PATHS = {-1: "auto", 0: "simt", 1: "tcgen05"}
 PATH_IDS = {"auto": -1, "simt": 0, "tcgen05": 1}
@@ -157,7 +157,10 @@ def effective_isa(kind: str, isa=None, m: int = 1, n: int | None = None, k: int 
     given) runs on with default params; the library's rule (capi.cu want_tc)."""
     pid = _path_id(isa)
     if pid == -1:
-        if kind == "w4a8":
+        if (kind != "w4a8" and n is not None and k is not None and (4 if kind == "mxfp4" else 8) <= m <= 16
+                and n * pad_to(k, MXBLOCK if kind == "mxfp4" else GROUP) <= 5e6):
+            pid = 0     # the few-token SIMT kernel (capi.cu want_tok)
+        elif kind == "w4a8":
             kp = pad_to(k, GROUP) if k is not None else 0
             big = n is not None and k is not None and n * kp >= 32e6
             pid = 1 if m >= 32 or (big and (m > 16 or (m >= 12 and kp > 8192))) else 0
