@@ -187,20 +187,24 @@ __global__ void __launch_bounds__(TOK_MAX_WARPS * 32) gemv_tok_kernel(const TokA
   }
 
   // partial sums of the warps meet in shared memory; warp order is fixed
-  float *mine = red + ((size_t)warp * 32 * R) * MT;
+  // partial sums of the warps meet in shared memory as red[warp][token][row]
+  // (consecutive rows in consecutive words: conflict-free stores and sums);
+  // warp order is fixed
+  float *mine = red + (size_t)warp * MT * 32 * R;
 #pragma unroll
-  for (int j = 0; j < R; ++j) {
-    float4 *d = reinterpret_cast<float4 *>(mine + (size_t)(32 * j + lane) * MT);
-    d[0] = make_float4(lo_f(yacc[j][0]), hi_f(yacc[j][0]), lo_f(yacc[j][1]), hi_f(yacc[j][1]));
-    d[1] = make_float4(lo_f(yacc[j][2]), hi_f(yacc[j][2]), lo_f(yacc[j][3]), hi_f(yacc[j][3]));
-  }
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      mine[(2 * p) * 32 * R + 32 * j + lane] = lo_f(yacc[j][p]);
+      mine[(2 * p + 1) * 32 * R + 32 * j + lane] = hi_f(yacc[j][p]);
+    }
   __syncthreads();
   for (int o = threadIdx.x; o < 32 * R * MT; o += blockDim.x) {
     // o = t * 32R + row: consecutive threads store consecutive rows of a token
     const int t = o / (32 * R), rl = o % (32 * R);
     const int n = blockIdx.x * 32 * R + rl, m = m0 + t;
     float s = 0.f;
-    for (int ww = 0; ww < W; ++ww) s += red[((size_t)ww * 32 * R + rl) * MT + t];
+    for (int ww = 0; ww < W; ++ww) s += red[(size_t)ww * MT * 32 * R + o];
     if (n < a.N && m < a.M) {
       if (a.ks == 1)
         a.y[(size_t)m * a.N + n] = s;
