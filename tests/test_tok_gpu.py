@@ -77,3 +77,17 @@ def test_tok_routing():
     assert K.describe_plan("w4a16", 17, 896, 896)["kernel"] != "tok"
     assert K.describe_plan("w4a16", 8, 896, 896, lb.Params(mr=4))["kernel"] == "staged"
     assert K.describe_plan("w4a8", 8, 896, 896)["kernel"] != "tok"
+
+
+def test_tok_k_ranges_alternating_shapes(rng):
+    """Calls with K ranges share one partial-sum buffer per stream:
+    alternating shapes repeat their first results exactly."""
+    cases = []
+    for m, n, k in ((16, 896, 4864), (8, 300, 11008), (16, 64, 2080), (9, 1500, 2048)):
+        W = lb.quantize_int4(rng.standard_normal((n, k)).astype(np.float32), asym=True).cuda()
+        x = torch.from_numpy(rng.standard_normal((m, W.kp)).astype(np.float32)).cuda()
+        assert K.describe_plan("w4a16", m, n, W.kp)["ksplit"] > 1
+        cases.append((x, W, K.gemm_w4a16(x, W).clone()))
+    for _ in range(3):
+        for x, W, y0 in cases:
+            assert torch.equal(K.gemm_w4a16(x, W), y0)
