@@ -45,6 +45,8 @@ extern "C" {
 #define LBC_PATH_AUTO (-1)
 #define LBC_PATH_SIMT 0    /* CUDA-core fp32 FMA (int32 dp4a for W4A8) */
 #define LBC_PATH_TCGEN05 1 /* tcgen05 tensor-core prefill path */
+#define LBC_PATH_MMA 3     /* warp-level tensor-core (mma.sync) decode, W4A16 1-2 tokens;
+                              2 is the reference's avx512 id and means auto */
 
 /* error codes: -1..-3 keep the reference's meaning */
 #define LBC_ERR_SHAPE (-1)  /* M,N,Kp <= 0, Kp % block, NULL pointer */

@@ -10,6 +10,7 @@
 #include <memory>
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include "../../include/lowbit_b200.h"
 #include "gemv_dispatch.cuh"
@@ -345,11 +346,81 @@ size_t w4a8_ws_layout(int M, int Kp, size_t *off_xs, size_t *off_asum, size_t *o
   return xq_bytes + xs_bytes + as_bytes + tc_bytes;
 }
 
+// automatic kernel choice: no path requested, or one of the reference's CPU
+// ISA ids (2 = avx512; 3 is this library's mma path)
+bool path_auto(const lbc_params *p) {
+  return !p || p->isa == LBC_PATH_AUTO || (p->isa >= 2 && p->isa != LBC_PATH_MMA);
+}
+
+// ------------------------------------------------------------------ tensor-core decode (mma.sync)
+// W4A16 with one or two tokens on the warp-level tensor-core kernel
+// (gemv_mma.cuh). Params on this path: nb = CTAs per SM (default 1), nr =
+// consumer warps per CTA (default 8), kb = K elements per ring stage (a
+// multiple of 128 x warps; default 4 groups per warp for one token, 2 for
+// two), order = ring stages (default 2 for one token; for two, as many as
+// fit beside the activation fragments in half an SM's shared memory, at
+// most 8). Measured on the 11008 x 4096 headline shape (CUDA graph of
+// rotating weight copies): one token 9.36 us at (8 warps, 4 groups, 2
+// stages), 10.6-12.3 us at other tilings, against 9.6 us for the
+// register-streamed SIMT kernel; two tokens 13.45 us against 14.35 us.
+struct MmaPlan {
+  int ntok = 1, nw = 8, jws = 2, ns = 4, grid = 1, smem = 0;
+};
+
+constexpr int MMA_MAX_STAGES = 8;
+
+int plan_mma(int fmt, int M, int N, int Kp, const lbc_params *p, MmaPlan &P) {
+  if (fmt != lbc::FMT_W4A16 || M > 2) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 with 1 or 2 tokens");
+  const DevInfo di = dev_info();
+  P.ntok = M;
+  P.nw = (p && p->nr > 0) ? p->nr : 8;
+  P.jws = (p && p->kb > 0) ? std::max(1, p->kb / (128 * P.nw)) : (M == 1 ? 4 : 2);
+  const int cps = (p && p->nb > 0) ? p->nb : 1;
+  P.grid = std::max(1, std::min(di.sms * cps, ceil_div(N, 16)));
+  if (!lbc::mma_combo(P.ntok, P.nw, P.jws)) return fail(LBC_ERR_PARAMS, "mma decode tile not compiled");
+  const int budget = di.smem_sm / 2 - 1024;
+  if (p && p->order > 0) {
+    P.ns = std::min(p->order, MMA_MAX_STAGES);
+  } else if (M == 1) {
+    P.ns = 2;
+  } else {
+    P.ns = MMA_MAX_STAGES;
+    while (P.ns > 2 && lbc::mma_smem_bytes(P.ntok, P.nw, P.jws, P.ns, Kp, N, P.grid) > budget) --P.ns;
+  }
+  P.smem = lbc::mma_smem_bytes(P.ntok, P.nw, P.jws, P.ns, Kp, N, P.grid);
+  if (P.smem > di.smem_optin) return fail(LBC_ERR_PARAMS, "mma decode: stages and activations do not fit in shared memory");
+  return 0;
+}
+
+// Requested explicitly (params.isa = LBC_PATH_MMA), or by the tuner. The
+// automatic choice keeps the register-streamed SIMT kernel for one and two
+// tokens: it is as fast or faster at one token, and the fused decode
+// prologues (RMSNorm, SiLU.up) of the model run on it, whose results must
+// equal the separate kernels' bit for bit.
+bool want_mma(const lbc_params *p, int fmt, int M, int N, int Kp) {
+  (void)fmt;
+  (void)M;
+  (void)N;
+  (void)Kp;
+  return p && p->isa == LBC_PATH_MMA;
+}
+
+int run_mma(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
+  MmaPlan P;
+  if (int rc = plan_mma(fmt, a.M, a.N, a.Kp, p, P)) return rc;
+  a.status = dev_info().status;
+  cudaError_t e = lbc::mma_launch(a, P.ntok, P.nw, P.jws, P.ns, P.grid, st);
+  if (e != cudaSuccess) return fail_cuda("mma decode gemv launch", e);
+  return LBC_PATH_MMA;
+}
+
 // ------------------------------------------------------------------ few-token path
 // Partial sums of the few-token kernel's K ranges: one grow-only buffer per
-// (device, stream), so a decode loop issues no allocation; while the stream
-// is being captured a growth is a stream-ordered allocation freed after the
-// launches
+// (device, stream), so a decode loop issues no allocation. A buffer once
+// handed out is never freed (a CUDA graph captured around an earlier call may
+// hold its address): a grown-out one is retired until the process exits, and
+// growth at least doubles. While the stream is being captured a growth is a
+// stream-ordered allocation freed after the launches.
 struct TokScratch {
   float *p;
   bool owned;
@@ -357,6 +428,7 @@ struct TokScratch {
 TokScratch tok_scratch(size_t bytes, cudaStream_t st) {
   static std::mutex mu;
   static std::unordered_map<uint64_t, std::pair<void *, size_t>> cache;
+  static std::vector<void *> retired;
   int d = 0;
   cudaGetDevice(&d);
   const uint64_t key = ((uint64_t)(d & 63) << 58) ^ (uint64_t)(uintptr_t)st;
@@ -373,16 +445,13 @@ TokScratch tok_scratch(size_t bytes, cudaStream_t st) {
     }
     return {static_cast<float *>(p), true};
   }
-  if (slot.first) {
-    cudaStreamSynchronize(st);
-    cudaFree(slot.first);
-    slot = {nullptr, 0};
-  }
-  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+  const size_t nb = std::max(bytes, 2 * slot.second);
+  if (cudaMalloc(&p, nb) != cudaSuccess) {
     cudaGetLastError();
     return {nullptr, false};
   }
-  slot = {p, bytes};
+  if (slot.first) retired.push_back(slot.first);
+  slot = {p, nb};
   return {static_cast<float *>(p), false};
 }
 
@@ -417,7 +486,7 @@ TokPlan tok_plan(int fmt, int M, int N, int Kp) {
 constexpr double LBC_TOK_MAX_WEIGHTS = 5e6;
 bool want_tok(const lbc_params *p, int fmt, int M, int N, int Kp) {
   if (fmt == lbc::FMT_W4A8) return false;
-  if (p && (p->isa != LBC_PATH_AUTO && p->isa < 2)) return false;
+  if (!path_auto(p)) return false;
   if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
   if (M > 16 || M < (fmt == lbc::FMT_MXFP4 ? 4 : 8)) return false;
   return (double)N * Kp <= LBC_TOK_MAX_WEIGHTS;
@@ -446,8 +515,7 @@ int run_tok(int fmt, const lbc::GemvArgs &a, cudaStream_t st) {
 // 10M weights up to 4 tokens, below 6M up to 31).
 bool want_tc(const lbc_params *p, int fmt, int M, int N, int Kp) {
   if (p && p->isa == LBC_PATH_TCGEN05) return true;
-  const bool automatic = !p || p->isa == LBC_PATH_AUTO || p->isa >= 2;
-  if (!automatic) return false;
+  if (!path_auto(p)) return false;
   if (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0 || p->nb > 0)) return false;
   // W4A8: the dp4a SIMT kernels up to 31 tokens (the decode kernel takes up
   // to 16 tokens on rows of up to 8192), except large matrices (32M+
@@ -522,6 +590,15 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
   if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
   if (int rc = device_gate()) return rc;
   const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
+  if (want_mma(p, fmt, M, N, Kp)) {
+    MmaPlan P;
+    if (int rc = plan_mma(fmt, M, N, Kp, p, P)) return rc;
+    if (buf && buflen > 0)
+      snprintf(buf, (size_t)buflen,
+               "{\"path\": \"mma\", \"kernel\": \"mma\", \"tokens\": %d, \"warps\": %d, \"units_per_stage\": %d, "
+               "\"stages\": %d, \"grid\": %d, \"smem\": %d}", P.ntok, P.nw, P.jws, P.ns, P.grid, P.smem);
+    return LBC_PATH_MMA;
+  }
   if (want_tok(p, fmt, M, N, Kp)) {
     const TokPlan P = tok_plan(fmt, M, N, Kp);
     if (buf && buflen > 0)
@@ -565,6 +642,12 @@ int lbc_gemm_w4a16(const float *x, int M, int Kp, const uint8_t *qw, const float
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_mma(p, lbc::FMT_W4A16, M, N, Kp)) {
+    lbc::GemvArgs a{};
+    a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+    a.M = M; a.N = N; a.Kp = Kp;
+    return run_mma(lbc::FMT_W4A16, a, p, static_cast<cudaStream_t>(stream));
+  }
   if (want_tok(p, lbc::FMT_W4A16, M, N, Kp)) {
     lbc::GemvArgs a{};
     a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
@@ -627,6 +710,7 @@ int lbc_gemm_w4a16_glu(const float *gu, int M, int Kp, const uint8_t *qw, const 
 int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8_t *e8m0, int N,
                    float *y, const lbc_params *p, void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_MXBLOCK)) return rc;
+  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 only");
   if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
@@ -664,6 +748,7 @@ int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int 
                     const uint8_t *qw, const float *scales, const uint8_t *zeros, int N, float *y,
                     const lbc_params *p, void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 only");
   if (!xq || !xs || !asum || !qw || !scales || !y || !al16(xq) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
@@ -689,6 +774,7 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
                   const uint8_t *zeros, int N, float *y, const lbc_params *p, void *workspace,
                   void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
+  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 only");
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))

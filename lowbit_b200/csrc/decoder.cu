@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <map>
+#include <vector>
 #include <mutex>
 #include <utility>
 
@@ -474,11 +475,14 @@ int lbc_qkv_rope(const float *qkv, const float *bias, const float *cos_t, const 
 namespace lbc {
 namespace {
 // Scratch of the key-split path, one grow-only buffer per (device, stream),
-// held until exit. It cannot grow inside a stream capture: a first call of
-// each shape outside the capture sizes it.
+// held until exit. A buffer once handed out is never freed (a CUDA graph of
+// an earlier step may hold its address): a grown-out one is retired until the
+// process exits, and growth at least doubles. It cannot grow inside a stream
+// capture: a first call of each shape outside the capture sizes it.
 float *att_workspace(size_t bytes, cudaStream_t st) {
   static std::mutex mu;
   static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
+  static std::vector<void *> retired;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
@@ -486,14 +490,11 @@ float *att_workspace(size_t bytes, cudaStream_t st) {
   if (slot.first && slot.second >= bytes) return static_cast<float *>(slot.first);
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
-  if (slot.first) {
-    cudaStreamSynchronize(st);  // the previous buffer may still be in use on this stream
-    cudaFree(slot.first);
-    slot = {nullptr, 0};
-  }
+  const size_t nb = std::max(bytes, 2 * slot.second);
   void *p = nullptr;
-  if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
-  slot = {p, bytes};
+  if (cudaMalloc(&p, nb) != cudaSuccess) return nullptr;
+  if (slot.first) retired.push_back(slot.first);
+  slot = {p, nb};
   return static_cast<float *>(p);
 }
 

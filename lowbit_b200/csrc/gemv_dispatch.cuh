@@ -36,6 +36,15 @@ cudaError_t rows_gather_launch(const GemvArgs &a, int mt, int ch, int r, dim3 gr
 cudaError_t rows_fused_launch(const GemvArgs &a, int xm, int mt, int ch, int r, dim3 grid, int threads,
                               cudaStream_t st);
 
+// Warp-level tensor-core decode kernel (gemv_mma.cuh), W4A16 with one or two
+// tokens: whether (tokens, consumer warps, units per warp per stage) is
+// instantiated, its dynamic shared memory with `ns` ring stages for a grid of
+// `grid` CTAs, its launch and its resident CTAs per SM
+bool mma_combo(int ntok, int nw, int jws);
+int mma_smem_bytes(int ntok, int nw, int jws, int ns, int Kp, int N, int grid);
+cudaError_t mma_launch(const GemvArgs &a, int ntok, int nw, int jws, int ns, int grid, cudaStream_t st);
+int mma_occupancy(int ntok, int nw, int jws, int smem);
+
 // thread-local note describing the last zero-occupancy configuration
 inline char *occ_note() {
   static thread_local char buf[160] = "";

@@ -69,7 +69,10 @@ cudaError_t scratch_address(void **out) {
 extern "C" int lbc_gemm_w4a8_noalloc(const float *x, int M, int Kp, const uint8_t *qw,
                                      const float *scales, const uint8_t *zeros, int N, float *y,
                                      const lbc_params *p, void *stream) {
-  if (M <= 0 || N <= 0 || Kp <= 0 || Kp % LBC_GROUP) return LBC_ERR_SHAPE;
+  if (M <= 0 || N <= 0 || Kp <= 0 || Kp % LBC_GROUP) {
+    lbc::set_last_error("lbc_gemm_w4a8_noalloc: bad shape (M, N, Kp must be positive, Kp a multiple of 128)");
+    return LBC_ERR_SHAPE;
+  }
   const size_t need = lbc_gemm_w4a8_workspace_size(M, Kp);
   if (need > (size_t)LBC_NOALLOC_SCRATCH_BYTES) {
     char msg[256];

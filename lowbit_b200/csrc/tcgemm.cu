@@ -4,6 +4,7 @@
 #include <chrono>
 #include <cstdio>
 #include <map>
+#include <vector>
 #include <mutex>
 #include <utility>
 
@@ -55,11 +56,16 @@ uint32_t next_epoch() {
 
 // Fixup scratch for calls without a workspace: one grow-only, zero-initialised
 // buffer per (device, stream), so back-to-back GEMMs on a stream issue no
-// allocation between them. The buffers live until the process exits. During
-// stream capture a growth falls back to a stream-ordered allocation.
+// allocation between them. A buffer once handed out is never freed: a CUDA
+// graph captured around an earlier call (the host-buffer entry points' cached
+// graphs, or a caller's own) holds its address, so a grown-out buffer is
+// retired, not released, and lives until the process exits; growth at least
+// doubles, so few are retired. During stream capture a growth falls back to
+// a stream-ordered allocation freed after the launches.
 void *cached_scratch(size_t need, cudaStream_t st, bool *owned) {
   static std::mutex mu;
   static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
+  static std::vector<void *> retired;
   *owned = false;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
@@ -77,18 +83,15 @@ void *cached_scratch(size_t need, cudaStream_t st, bool *owned) {
     *owned = true;
     return p;
   }
-  if (slot.first) {
-    cudaStreamSynchronize(st);
-    cudaFree(slot.first);
-    slot = {nullptr, 0};
-  }
+  const size_t bytes = std::max(need, 2 * slot.second);
   void *p = nullptr;
-  if (cudaMalloc(&p, need) != cudaSuccess) {
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
     cudaGetLastError();
     return nullptr;
   }
-  cudaMemsetAsync(p, 0, need, st);
-  slot = {p, need};
+  cudaMemsetAsync(p, 0, bytes, st);
+  if (slot.first) retired.push_back(slot.first);
+  slot = {p, bytes};
   return p;
 }
 

@@ -36,7 +36,9 @@
 //   * a tile split between CTAs is finished without zeroing Y or atomics: a CTA
 //     whose range starts inside a tile writes its partial rows to a workspace
 //     slot and raises a per-call epoch flag; the CTA owning the tile's first
-//     units (it reaches that tile last) adds the partials and stores Y.
+//     units (it reaches that tile last) adds the partials, stores Y and clears
+//     each flag it has seen, so a replay of a captured launch (same epoch)
+//     finds every flag clear.
 #pragma once
 
 #include <cuda.h>
@@ -574,6 +576,11 @@ __global__ void __maxnreg__(80) tcgemm_kernel(const __grid_constant__ CUtensorMa
                 break;
               }
             }
+            // clear the flag once seen: a CUDA graph replays this launch with the
+            // same epoch, and must find every flag clear until its own producer
+            // CTA raises it (the next launch's producers write flags only after
+            // griddepcontrol.wait, i.e. after this kernel has completed)
+            if (seen) *const_cast<volatile uint32_t *>(f) = 0u;
           }
           named_bar_sync(3, 128);
           const float *src = a.partial + ((size_t)chunk * NCTA + c) * (TC_ROWS * MT) + row * MT;

@@ -11,8 +11,9 @@ error behaviour) with the computation on the GPU:
 * ``params`` is a :class:`Params` (fields reinterpreted for the GPU, see
   include/lowbit_b200.h), ``None`` or ``"auto"`` (tuned cache, lowbit_b200.tune);
 * ``isa`` selects the kernel path: None/"auto" (one or two tokens: the SIMT
-  decode kernels; more: the tcgen05 tensor-core kernel,
-  for W4A8 from 32 tokens), "simt", "tcgen05"; the reference's CPU ISA names
+  decode kernels; more: the tcgen05 tensor-core kernel, for W4A8 from 32
+  tokens), "simt", "tcgen05", "mma" (the warp-level tensor-core decode
+  kernel, W4A16 with one or two tokens); the reference's CPU ISA names
   ("scalar", "avx2", "avx512") are accepted and mean "auto". Explicit tiling
   fields in ``params`` (mr, nr, nb, kb, order) keep "auto" on the SIMT kernels;
 * ``threads`` is accepted and ignored (CPU thread count).
@@ -32,8 +33,8 @@ import numpy as np
 from ._build import build
 from .formats import GROUP, MXBLOCK, Int4Weights, Int8Acts, MXFP4Weights, pad_to
 
-PATHS = {-1: "auto", 0: "simt", 1: "tcgen05"}
-PATH_IDS = {"auto": -1, "simt": 0, "tcgen05": 1}
+PATHS = {-1: "auto", 0: "simt", 1: "tcgen05", 3: "mma"}
+PATH_IDS = {"auto": -1, "simt": 0, "tcgen05": 1, "mma": 3}
 REFERENCE_ISAS = ("scalar", "avx2", "avx512")
 KIND_IDS = {"w4a16": 0, "mxfp4": 1, "w4a8": 2}
 ERR_NAMES = {-1: "bad shape or pointer", -2: "tile parameters not supported", -3: "allocation failed",

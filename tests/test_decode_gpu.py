@@ -33,6 +33,8 @@ def test_decode_plan_is_rows(m, k):
         assert plan["kernel"] == ("rows" if fits else "staged"), plan
         if fits:
             assert plan["mt"] == m, plan
+        plan = K.describe_plan(kind, m, 300, kp, isa="simt")
+        assert plan["kernel"] == ("rows" if fits else "staged"), plan
     # MXFP4 takes the decode kernel for one token only
     plan = K.describe_plan("mxfp4", m, 300, kp)
     assert plan["kernel"] == ("rows" if fits and m == 1 else "staged"), plan
@@ -45,9 +47,10 @@ def test_decode_w4a16(rng, m, k, n):
     x, w = _problem(rng, m, n, k)
     for asym in (False, True):
         W = lb.quantize_int4(w, asym=asym)
-        y = K.gemm_w4a16(x, W)
-        R.assert_close(y, R.gemm_w4a16_ref(x, W.qw, W.scales, W.zeros),
-                       R.abs_bound(x, R.dequant_int4(W.qw, W.scales, W.zeros)), RTOL)
+        for isa in (None, "simt"):
+            y = K.gemm_w4a16(x, W, isa=isa)
+            R.assert_close(y, R.gemm_w4a16_ref(x, W.qw, W.scales, W.zeros),
+                           R.abs_bound(x, R.dequant_int4(W.qw, W.scales, W.zeros)), RTOL)
 
 
 @pytest.mark.parametrize("m", [1, 2])

@@ -116,3 +116,28 @@ def test_host_entry_bad_arguments():
     assert L.lbc_gemm_mxfp4_host(x.ctypes.data, 1, 100, None, None, 16, x.ctypes.data, None, None) == -1
     assert L.lbc_gemm_w4a8_host(x.ctypes.data, 0, 128, None, None, None, 16, x.ctypes.data, None, None) == -1
     assert C.c_int(L.lbc_device_status(1)).value == 0
+
+
+@pytest.mark.parametrize("kind", ["w4a16", "mxfp4"])
+def test_host_scratch_growth_keeps_cached_graphs_valid(rng, kind):
+    """A cached host-call graph holds the address of the per-stream scratch its
+    capture used (tensor-core fixup slots, few-token K-range partial sums). A
+    later call that needs more scratch grows it; the earlier graph must still
+    see valid memory when it is replayed: small key, big key, small key
+    again, each equal to the device path. Shapes: few-token kernel with K
+    ranges (8 tokens on 896 x 4864, then 16 tokens on 1152 x 4864) and the
+    tensor-core exact kernel (32 tokens on 4096 x 4096, then 48 on 11008 x 4096)."""
+    quant, fn = KINDS[kind]
+    for (m1, n1, k1), (m2, n2, k2) in (((8, 896, 4864), (16, 1152, 4864)),
+                                       ((32, 4096, 4096), (48, 11008, 4096))):
+        xs = rng.standard_normal((m1, k1)).astype(np.float32)
+        xb = rng.standard_normal((m2, k2)).astype(np.float32)
+        Ws = quant(rng.standard_normal((n1, k1)).astype(np.float32))
+        Wb = quant(rng.standard_normal((n2, k2)).astype(np.float32))
+        ref_s, ref_b = _device(fn, xs, Ws), _device(fn, xb, Wb)
+        for _ in range(2):      # eager + capture of the small key
+            np.testing.assert_array_equal(fn(xs, Ws), ref_s)
+        for _ in range(2):      # the big key grows the scratch
+            np.testing.assert_array_equal(fn(xb, Wb), ref_b)
+        for _ in range(3):      # the small key's cached graph again
+            np.testing.assert_array_equal(fn(xs, Ws), ref_s)

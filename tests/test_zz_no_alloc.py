@@ -50,12 +50,19 @@ def _run_both(L, x, W):
     return y_ref.cpu().numpy(), y_na.cpu().numpy()
 
 
+# (M, N, K, asym): the SIMT decode kernels (16 and 3 tokens) and, at 32 tokens
+# on a 4096 x 4096 matrix, the tensor-core exact kernel, whose partial-row
+# slots and epoch flags also live in the static scratch
+CASES = [(16, 256, 4096, False), (3, 96, 640, True), (32, 4096, 4096, True), (16, 256, 4096, False),
+         (32, 4096, 4096, True)]
+
+
 def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     L = _lib()
     rng = np.random.default_rng(99)
-    # two different problems in a row: the second reuses (and must not depend
-    # on) what the first left in the static scratch
-    for (m, n, k, asym) in [(16, 256, 4096, False), (3, 96, 640, True), (16, 256, 4096, False)]:
+    # different problems in a row: each reuses (and must not depend on) what
+    # the one before left in the static scratch
+    for (m, n, k, asym) in CASES:
         x = (rng.standard_normal((m, k)) * rng.uniform(0.1, 10)).astype(np.float32)
         W = lb.quantize_int4(rng.standard_normal((n, k)).astype(np.float32), asym=asym)
         y_ref, y_na = _run_both(L, x, W)
@@ -73,3 +80,41 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     rc = L.lbc_gemm_w4a8_noalloc(None, m, kp, None, None, None, 16, None, None, None)
     assert rc == -1
     assert b"static buffer" in L.lbc_last_error()
+
+
+def test_noalloc_allocates_nothing():
+    """After a first round (which may load kernels lazily), more calls leave the
+    device's free memory and torch's allocator unchanged."""
+    import torch
+    L = _lib()
+    rng = np.random.default_rng(7)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = torch.cuda.current_stream().cuda_stream
+    probs = []
+    for (m, n, k, asym) in CASES[:3]:
+        W = lb.quantize_int4(rng.standard_normal((n, k)).astype(np.float32), asym=asym)
+        xd = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to(dev)
+        probs.append((m, n, k, xd, torch.from_numpy(W.qw).to(dev), torch.from_numpy(W.scales).to(dev),
+                      None if W.zeros is None else torch.from_numpy(W.zeros).to(dev),
+                      torch.empty((m, n), device=dev)))
+
+    def round_():
+        for (m, n, k, xd, qw, sc, zz, y) in probs:
+            rc = L.lbc_gemm_w4a8_noalloc(xd.data_ptr(), m, k, qw.data_ptr(), sc.data_ptr(),
+                                         None if zz is None else zz.data_ptr(), n, y.data_ptr(), None, st)
+            assert rc >= 0, L.lbc_last_error()
+        torch.cuda.synchronize()
+
+    round_()
+    free0, alloc0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
+    for _ in range(3):
+        round_()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_allocated() == alloc0
+
+
+def test_noalloc_bad_shape_sets_error_text():
+    L = _lib()
+    rc = L.lbc_gemm_w4a8_noalloc(None, 0, 128, None, None, None, 16, None, None, None)
+    assert rc == -1
+    assert b"bad shape" in L.lbc_last_error()
