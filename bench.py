@@ -63,6 +63,7 @@ METRIC = "M=1 decode weight GB/s (W4A16 int4-g128 asym, N=11008, K=4096)"
 WORKLOAD = "W4A16 decode GEMM M=1 N=11008 K=4096, int4 g128 asym (BASELINE configs[0])"
 PUBLISHED_GBPS = 22.4  # reference README: W4A16 M=1 N=11008 K=4096 cold, AVX-512, 4 threads
 FALLBACK_HBM_GBS = 6650.0
+REPLAYS = 10  # timed replays of the step graph; the line reports their median
 
 
 def peaks() -> tuple[float, float, float, str]:
@@ -78,6 +79,38 @@ def inputs(m=M, n=N, k=K):
     w = np.random.default_rng(0).standard_normal((n, k)).astype(np.float32)
     x = np.random.default_rng(1).standard_normal((m, k)).astype(np.float32)
     return x, w
+
+
+def _sha(*arrays) -> str:
+    """SHA-256 of arrays as tests/golden/make_golden.py records them."""
+    import hashlib
+    h = hashlib.sha256()
+    for a in arrays:
+        if a is None:
+            h.update(b"none")
+        else:
+            a = np.ascontiguousarray(a)
+            h.update(str(a.dtype).encode() + str(a.shape).encode())
+            h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def reference_weights(name: str, fmt: str, w: np.ndarray, asym: bool = False):
+    """Packed weights for the reference's CPU kernels, in the bytes lowbit's own
+    quantizer produces: quantized here, then checked against the SHA-256 the
+    reference recorded for the same BASELINE input (tests/golden/
+    golden_meta.json, written by tests/golden/make_golden.py from lowbit).
+    Returns (weights, note); the note says whether the digest matched."""
+    from lowbit_b200 import quantize_int4, quantize_mxfp4
+    W = quantize_mxfp4(w) if fmt == "mxfp4" else quantize_int4(w, asym=asym)
+    arrays = (W.qw, W.e8m0) if fmt == "mxfp4" else (W.qw, W.scales, W.zeros)
+    try:
+        want = json.loads((ROOT / "tests" / "golden" / "golden_meta.json").read_text())["digests"][name + "_packed"]
+    except (OSError, KeyError, ValueError):
+        return W, "packed bytes not checked (no golden digest)"
+    if _sha(*arrays) != want:
+        raise SystemExit(f"packed {name} weights differ from the reference quantizer's (digest mismatch)")
+    return W, "packed bytes equal to lowbit's quantizer output (SHA-256 of tests/golden/golden_meta.json)"
 
 
 # ---------------------------------------------------------------- clocks
@@ -136,13 +169,12 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- reference arm
 def run_reference(args) -> dict:
-    from lowbit_b200 import quantize_int4
     from oracle import ref_lib
     if not ref_lib.available():
         return {"impl": "reference", "unavailable": "oracle/_ref/liblowbit_ref.so not built "
                 "(make -C oracle ref needs the reference sources)"}
     x, w = inputs()
-    W = quantize_int4(w, asym=True)
+    W, wnote = reference_weights("w4a16_decode", "w4a16", w, asym=True)
     threads = os.cpu_count() or 1
     g = ref_lib.RefGemm("w4a16", x, W, threads)
     info = g.info()
@@ -161,7 +193,7 @@ def run_reference(args) -> dict:
     gbps = W.nbytes / (total / args.steps) / 1e9
     sample = (f"lowbit lb_gemm_w4a16 ({info['isa']}, openmp={info['openmp']}) M=1 N=11008 K=4096, "
               f"{args.steps} calls, cold: {len(pool)} weight copies rotated, tuned params "
-              f"mr={g.params.mr} nr={g.params.nr} nb={g.params.nb} kb={g.params.kb}")
+              f"mr={g.params.mr} nr={g.params.nr} nb={g.params.nb} kb={g.params.kb}; {wnote}")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbps, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -187,13 +219,12 @@ def _host_pool(W):
 
 def cpu_baseline(budget_s: float = 10.0) -> dict:
     """The reference's CPU kernel on the host cores, bounded sample (rank 0, N=1)."""
-    from lowbit_b200 import quantize_int4
     from oracle import ref_lib
     if not ref_lib.available():
         return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference",
                 "sample": "unavailable: oracle/_ref/liblowbit_ref.so not built"}
     x, w = inputs()
-    W = quantize_int4(w, asym=True)
+    W, wnote = reference_weights("w4a16_decode", "w4a16", w, asym=True)
     threads = os.cpu_count() or 1
     g = ref_lib.RefGemm("w4a16", x, W, threads)
     info = g.info()
@@ -212,7 +243,7 @@ def cpu_baseline(budget_s: float = 10.0) -> dict:
     return {"value": round(W.nbytes / med / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
             "sample": f"lowbit lb_gemm_w4a16 ({info['isa']}, openmp={info['openmp']}) M=1 N=11008 K=4096, "
                       f"median of {len(ts)} cold calls over {budget_s:.0f} s, tuned mr={g.params.mr} "
-                      f"nr={g.params.nr} nb={g.params.nb} kb={g.params.kb}"}
+                      f"nr={g.params.nr} nb={g.params.nb} kb={g.params.kb}; {wnote}"}
 
 
 # ---------------------------------------------------------------- our arm
@@ -310,33 +341,28 @@ def run_ours(args) -> dict | None:
         g_gemv.replay()
         torch.cuda.synchronize()
 
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    ev0.record()
-    g_step.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    barrier()
-    ms_step_local = ev0.elapsed_time(ev1) / args.steps
+    def timed(graph, reps=REPLAYS):
+        """Median over `reps` replays of a graph of args.steps steps, ms per step
+        (CUDA events on the replaying stream, barrier + synchronize around each)."""
+        out = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            torch.cuda.synchronize()
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            out.append(e0.elapsed_time(e1) / args.steps)
+        barrier()
+        return statistics.median(out)
 
+    ms_step_local = timed(g_step)
     # kernel-only duration (no collective) for the roofline
-    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    ev2.record()
-    g_gemv.replay()
-    ev3.record()
-    torch.cuda.synchronize()
-    ms_kernel_local = ev2.elapsed_time(ev3) / args.steps
+    ms_kernel_local = timed(g_gemv)
     ms_nccl_local = 0.0
     if g_nccl is not None:
-        barrier()
-        torch.cuda.synchronize()
-        ev2.record()
-        g_nccl.replay()
-        ev3.record()
-        torch.cuda.synchronize()
-        ms_nccl_local = ev2.elapsed_time(ev3) / args.steps
+        ms_nccl_local = timed(g_nccl)
     clk = clocks.stop()
 
     t = torch.tensor([ms_step_local, ms_kernel_local, ms_nccl_local], device=dev)
@@ -398,7 +424,7 @@ def run_ours(args) -> dict | None:
                    "parallelism": f"N-shard x{world}" + (" + all-gather of Y fused into the GEMV (NVLink peer stores)"
                                                         if world > 1 else ""),
                    "l2": f"inputs larger than L2: {copies} rotating weight copies ({pool_mb:.0f} MB/rank)",
-                   "timing": "K steps in one CUDA graph replay, CUDA events, max over ranks"},
+                   "timing": f"K steps in one CUDA graph, CUDA events, median of {REPLAYS} replays, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": traffic, "peak_source": peak_src,
                      "alg_bytes_per_launch": alg_bytes, "kernel_us": round(ms_kernel * 1e3, 3)},
@@ -413,7 +439,70 @@ def run_ours(args) -> dict | None:
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_seconds)
+    if world == 1 and not args.no_secondary:
+        line["secondary"] = secondary_lines(args)
     return line
+
+
+# BASELINE configs[1] and [2] and the prefill kernel's target shape, reported
+# beside the headline: (name, format, M, N, K, golden digest name, asym)
+SECONDARY = (("w4a8_m16", "w4a8", 16, 4096, 4096, "w4a8_m16", False),
+             ("mxfp4_m64", "mxfp4", 64, 11008, 4096, "mxfp4_m64", False),
+             ("w4a16_prefill_m4096", "w4a16", 4096, 11008, 4096, "w4a16_decode", True))
+
+
+def _median_time(fn, budget_s: float, min_calls: int = 3) -> tuple[float, int]:
+    fn()
+    ts = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(ts) < min_calls:
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts), len(ts)
+
+
+def secondary_cpu(name: str, fmt: str, m: int, n: int, k: int, digest: str, asym: bool, budget_s: float) -> dict:
+    """The reference's best CPU path for one secondary shape on all host cores,
+    median over a bounded sample: W4A8 both the VNNI kernel (tuned) and the
+    AMX kernel (when this host has AMX), reporting the faster; MXFP4 its
+    AVX-512 kernel (tuned); W4A16 at 4096 tokens its AVX-512 kernel with the
+    default tiles (one call takes seconds: no tuning)."""
+    from lowbit_b200.formats import pack_amx
+    from oracle import ref_lib
+    if not ref_lib.available():
+        return {"value": None, "unit": "us", "cores": 0, "kind": "reference",
+                "sample": "unavailable: oracle/_ref/liblowbit_ref.so not built"}
+    w = np.random.default_rng(0).standard_normal((n, k)).astype(np.float32)
+    x = np.random.default_rng(1).standard_normal((m, k)).astype(np.float32)
+    W, wnote = reference_weights(digest, fmt, w, asym=asym)
+    threads = os.cpu_count() or 1
+    g = ref_lib.RefGemm(fmt, x, W, threads)
+    info = g.info()
+    paths = {}
+    if m <= 64:
+        g.tune(budget_s=min(3.0, budget_s / 2))
+    t, calls = _median_time(g, budget_s / 2)
+    paths[f"{info['isa']}{'+vnni' if fmt == 'w4a8' and info['vnni'] else ''}"] = (t, calls)
+    if fmt == "w4a8" and ref_lib.amx_available():
+        ga = ref_lib.RefGemmAMX(x, pack_amx(W), threads)
+        paths["amx"] = _median_time(ga, budget_s / 2)
+    best = min(paths, key=lambda p: paths[p][0])
+    return {"value": round(paths[best][0] * 1e6, 1), "unit": "us", "cores": threads, "kind": "reference",
+            "path": best, "paths_us": {p: round(v[0] * 1e6, 1) for p, v in paths.items()},
+            "sample": f"lowbit {fmt} M={m} N={n} K={k} on {threads} threads: median of "
+                      f"{', '.join(f'{v[1]} {p} calls' for p, v in paths.items())} (openmp={info['openmp']}); {wnote}"}
+
+
+def secondary_lines(args) -> dict:
+    out = {}
+    for name, fmt, m, n, k, digest, asym in SECONDARY:
+        steps = max(5, min(args.steps, int(2e6 / (m * n * k / 1e6 + 50))))
+        line = gemm_line(fmt, m, n, k, steps, 3)
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = secondary_cpu(name, fmt, m, n, k, digest, asym, args.cpu_seconds / 2)
+        out[name] = line
+    return out
 
 
 def Kn_x_bytes(kp: int) -> int:
@@ -436,17 +525,62 @@ SWEEP_M = (1, 16, 64, 512, 4096)
 SWEEP_NK = ((4096, 4096), (11008, 4096), (4096, 11008), (14336, 4096))
 
 
-def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int) -> dict:
-    """One GEMM of `fmt` (w4a16 asym / w4a8 sym / mxfp4) on seeded N(0,1) inputs,
-    device-resident, timed as a CUDA graph of `steps` calls over rotating
-    weight copies (inputs + copies larger than L2), CUDA events."""
+_INPUTS: dict = {}
+
+
+def _gemm_inputs(m: int, n: int, k: int):
+    """BASELINE.json's inputs: W [N, K] ~ N(0, 1) from numpy default_rng(0), X
+    [M, K] ~ N(0, 1) from default_rng(1), generated on the host (cached per
+    shape within a run)."""
+    if (n, k) not in _INPUTS:
+        _INPUTS[(n, k)] = np.random.default_rng(0).standard_normal((n, k)).astype(np.float32)
+    if (m, k) not in _INPUTS:
+        _INPUTS[(m, k)] = np.random.default_rng(1).standard_normal((m, k)).astype(np.float32)
+    return _INPUTS[(n, k)], _INPUTS[(m, k)]
+
+
+def _gemm_check(fmt: str, x: np.ndarray, W, y, plan: dict) -> float:
+    """One oracle check of a timed GEMM (outside the timing): up to 64 sampled
+    weight rows x 256 sampled tokens in float64; tolerance 4e-3 * (|X| . |W|^T)
+    on the bf16 prefill kernel (W4A16 / MXFP4 from 64 tokens), 1e-5 on the
+    exact paths, the W4A8 magnitude bound for W4A8. Returns max err / limit."""
+    from oracle import lbref as R
+    rng = np.random.default_rng(3)
+    m, n = y.shape
+    rows = np.sort(rng.choice(n, min(n, 64), replace=False))
+    toks = np.sort(rng.choice(m, min(m, 256), replace=False))
+    import torch
+    ti, ri = torch.as_tensor(toks, device=y.device), torch.as_tensor(rows, device=y.device)
+    ys = y[ti][:, ri].cpu().numpy()
+    xs = x[toks]
+    qw = W.qw[ri].cpu().numpy()
+    if fmt == "mxfp4":
+        e = W.e8m0[ri].cpu().numpy()
+        tol = 4e-3 if plan.get("kernel") == "prefill" else 1e-5
+        return R.assert_close(ys, R.gemm_mxfp4_ref(xs, qw, e), R.abs_bound(xs, R.dequant_mxfp4(qw, e)), tol)
+    sc = W.scales[ri].cpu().numpy()
+    z = None if W.zeros is None else W.zeros[ri].cpu().numpy()
+    if fmt == "w4a16":
+        tol = 4e-3 if plan.get("kernel") == "prefill" else 1e-5
+        return R.assert_close(ys, R.gemm_w4a16_ref(xs, qw, sc, z), R.abs_bound(xs, R.dequant_int4(qw, sc, z)), tol)
+    xq, xsc, asum = R.quant_act_int8_ref(xs, W.kp)
+    return R.assert_close(ys, R.gemm_w4a8_ref(xq, xsc, asum, qw, sc, z), R.w4a8_bound(xq, xsc, asum, qw, sc, z), 1e-5)
+
+
+def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int, reps: int = 10) -> dict:
+    """One GEMM of `fmt` (w4a16 asym / w4a8 sym / mxfp4) on BASELINE's seeded
+    inputs (numpy seeds 0 / 1, quantized on the GPU bit-identically to the
+    reference's quantizers), device-resident, checked once against the
+    oracle, then timed as a CUDA graph of `steps` calls over rotating weight
+    copies (inputs + copies larger than L2), CUDA events, median of `reps`
+    replays."""
     import torch
     from lowbit_b200 import kernels as Kn
     from lowbit_b200.kernels import quantize_int4_cuda, quantize_mxfp4_cuda
     hbm, tf_burst, tf_sust, src = peaks()
-    g = torch.Generator(device="cuda").manual_seed(0)
-    w = torch.randn(n, k, device="cuda", generator=g)
-    x = torch.randn(m, k, device="cuda", generator=g)
+    wh, xh = _gemm_inputs(m, n, k)
+    w = torch.from_numpy(wh).cuda()
+    x = torch.from_numpy(xh).cuda()
     W = (quantize_mxfp4_cuda(w) if fmt == "mxfp4" else quantize_int4_cuda(w, asym=(fmt == "w4a16")))
     del w
     wbytes = int(sum(t.numel() * t.element_size() for t in
@@ -457,6 +591,10 @@ def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int) -> dict
                                 if getattr(W, f, None) is not None}) for _ in range(copies - 1)]
     fn = {"w4a16": Kn.gemm_w4a16, "w4a8": Kn.gemm_w4a8, "mxfp4": Kn.gemm_mxfp4}[fmt]
     prep = Kn._Prepared(x, W.kp, n)
+    plan = Kn.describe_plan(fmt, m, n, W.kp)
+    fn(x, W, _prep=prep)
+    torch.cuda.synchronize()
+    parity = _gemm_check(fmt, xh, W, prep.y, plan)
     for i in range(warmup):
         fn(x, pool[i % copies], _prep=prep)
     torch.cuda.synchronize()
@@ -466,24 +604,27 @@ def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int) -> dict
             fn(x, pool[i % copies], _prep=prep)
     graph.replay()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-    e0.record()
-    graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / steps
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3 / steps)
+    us = statistics.median(ts)
     flops = 2.0 * m * n * k
     byts = wbytes + 4 * m * W.kp + 4 * m * n
     peak_t = tf_burst * (2 if fmt == "w4a8" else 1)
     tensor_bound = flops / (peak_t * 1e12) > byts / (hbm * 1e9)
-    plan = Kn.describe_plan(fmt, m, n, W.kp)
     ach = flops / us / 1e6 if tensor_bound else byts / us / 1e3
     peak = peak_t if tensor_bound else hbm
     return {"fmt": fmt, "M": m, "N": n, "K": k, "us": round(us, 3), "TFLOP/s": round(flops / us / 1e6, 2),
             "GB/s": round(byts / us / 1e3, 1), "kernel": plan.get("kernel", plan.get("path")),
+            "parity": {"max_err_over_limit": round(parity, 4), "sample": "64 weight rows x 256 tokens, float64 oracle"},
             "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": round(ach, 2),
                          "peak": peak, "unit": "TFLOP/s" if tensor_bound else "GB/s", "frac": round(ach / peak, 4),
-                         "peak_source": src + (" (int8: 2x the bf16 figure, not measured)"
+                         "peak_source": src + (" (int8: 2x the bf16 figure, assumed: not measured)"
                                                if tensor_bound and fmt == "w4a8" else "")},
             "weight_copies": copies}
 
@@ -495,9 +636,11 @@ def run_gemm(args) -> dict:
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
             "dtype": {"w4a16": "f32 (bf16 from 64 tokens)", "w4a8": "int8/int32",
                       "mxfp4": "f32 (bf16 from 64 tokens)"}[args.fmt],
-            "data": "synthetic: W, X ~ N(0,1) (torch seed 0), quantized on the GPU",
+            "data": "synthetic: W ~ N(0,1) numpy default_rng(0), X ~ N(0,1) default_rng(1), quantized on the GPU "
+                    "bit-identically to the reference's quantizers",
             "config": {"workload": f"{args.fmt} GEMM M={args.m} N={args.n} K={args.k}",
-                       "timing": "CUDA graph of `steps` calls over rotating weight copies, CUDA events"},
+                       "timing": "CUDA graph of `steps` calls over rotating weight copies, CUDA events, "
+                                 "median of 10 replays"},
             "detail": line}
 
 
@@ -642,6 +785,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="omit the secondary block (configs[1], configs[2], M=4096 prefill)")
     ap.add_argument("--workload", choices=["decode", "model", "gemm", "sweep"], default="decode")
     ap.add_argument("--fmt", choices=["w4a16", "w4a8", "mxfp4"], default="w4a16")
     ap.add_argument("--m", type=int, default=4096)

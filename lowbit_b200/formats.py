@@ -286,3 +286,65 @@ def quantize_act_int8(x: np.ndarray, kp: int | None = None) -> Int8Acts:
     q = np.clip(np.rint(xp / s[:, None]), -127, 127).astype(np.int8)
     gsum = q.reshape(q.shape[0], -1, GROUP).astype(np.int32).sum(axis=2, dtype=np.int32)
     return Int8Acts(q, s, gsum)
+
+
+# ---------------------------------------------------------------- AMX repack (drop-in)
+
+@dataclass
+class AMXInt4Weights:
+    """int4 g128 weights in the layout of lowbit's AMX tile kernel
+    (src/lowbit/formats.py:251-293), kept byte for byte so that weights a
+    lowbit caller repacked with its `pack_amx` are accepted unchanged.
+
+    Per block of 16 output rows and group g: 1 KiB where byte (r, 4c + i) holds
+    the code of row n0 + c at element 128g + 4r + i (low nibble) and at
+    128g + 64 + 4r + i (high nibble); scales s, s * z and z as [NB, G, 16].
+    On the GPU these weights run the W4A8 kernels in the canonical layout:
+    `to_int4()` undoes the repack exactly (padding rows dropped)."""
+    qw: np.ndarray      # uint8 [NB * G * 1024]
+    scales: np.ndarray  # float32 [NB, G, 16]
+    sz: np.ndarray      # float32 [NB, G, 16]  = s * z
+    zeros: np.ndarray   # uint8 [NB, G, 16]
+    n: int
+    k: int
+    kp: int
+
+    @property
+    def nbytes(self) -> int:
+        return self.qw.nbytes + self.scales.nbytes + self.sz.nbytes
+
+    def to_int4(self) -> Int4Weights:
+        """The canonical Int4Weights these bytes were packed from: byte (r, c, i)
+        of block b, group g is byte j = 4r + i of row 16b + c's group g (the
+        canonical layout puts element 128g + j in the low nibble of that byte and
+        128g + 64 + j in the high one, as the AMX layout does)."""
+        nb, g = self.scales.shape[0], self.kp // GROUP
+        b = np.asarray(self.qw, np.uint8).reshape(nb, g, 16, 16, 4)          # [nb, g, r, c, i]
+        qw = np.ascontiguousarray(b.transpose(0, 3, 1, 2, 4)).reshape(nb * 16, g * 64)[: self.n]
+        sc = np.ascontiguousarray(np.asarray(self.scales, np.float32).transpose(0, 2, 1)).reshape(nb * 16, g)
+        z = np.ascontiguousarray(np.asarray(self.zeros, np.uint8).transpose(0, 2, 1)).reshape(nb * 16, g)
+        return Int4Weights(qw, sc[: self.n].copy(), z[: self.n].copy(), self.k)
+
+
+def pack_amx(w: Int4Weights) -> AMXInt4Weights:
+    """The AMX repack of lowbit (src/lowbit/formats.py:275-293): rows padded to
+    a multiple of 16 with codes equal to their zero point (they decode to 0)."""
+    n, kp = w.n, w.kp
+    g = kp // GROUP
+    nb = -(-n // 16)
+    z = np.full((nb * 16, g), 8, np.uint8)
+    if w.zeros is not None:
+        z[:n] = _np(w.zeros)
+    s = np.zeros((nb * 16, g), np.float32)
+    s[:n] = _np(w.scales)
+    # canonical bytes of padding rows: both nibbles = z
+    qw = np.empty((nb * 16, kp // 2), np.uint8)
+    qw[:n] = _np(w.qw)
+    qw[n:] = np.repeat(z[n:] * np.uint8(17), 64, axis=1)
+    # [nb, c, g, r, i] -> [nb, g, r, c, i]
+    packed = qw.reshape(nb, 16, g, 16, 4).transpose(0, 2, 3, 1, 4)
+    sb = np.ascontiguousarray(s.reshape(nb, 16, g).transpose(0, 2, 1))
+    zb = np.ascontiguousarray(z.reshape(nb, 16, g).transpose(0, 2, 1))
+    return AMXInt4Weights(np.ascontiguousarray(packed).reshape(-1), sb,
+                          (sb * zb.astype(np.float32)).astype(np.float32), zb, n, w.k, kp)
+

@@ -140,7 +140,7 @@ def cpu_info() -> dict:
     """lowbit.cpu_info() compatibility: the keys callers read, describing the GPU backend."""
     g = gpu_info()
     return {"cpu_isa": "sm_100a", "active_isa": "sm_100a", "vnni": False, "openmp": False,
-            "max_threads": 1, "amx": False, "gpu": g}
+            "max_threads": 1, "amx": True, "gpu": g}
 
 
 def _path_id(isa) -> int:
@@ -378,6 +378,42 @@ def gemm_w4a8(x, w: Int4Weights, params: Params | None = None, isa=None,
                                pr.y.data_ptr(), _pref(params, isa, "w4a8", pr.m, n, w.k), ws.data_ptr(),
                                _raw_stream(pr.x.device.index)), "lbc_gemm_w4a8")
     return pr.result()
+
+
+def amx_available() -> bool:
+    """lowbit.kernels.amx_available(): the AMX entry points are served by the
+    GPU's W4A8 kernels here, so they are always available."""
+    return True
+
+
+def _amx_int4(w) -> Int4Weights:
+    """Canonical device weights of AMX-packed ones (unpacked once, cached on the object)."""
+    c = getattr(w, "_lbc_int4", None)
+    if c is None:
+        from .formats import AMXInt4Weights
+        if not hasattr(w, "to_int4"):   # a lowbit.AMXInt4Weights: same fields and bytes
+            w = AMXInt4Weights(w.qw, w.scales, w.sz, w.zeros, w.n, w.k, w.kp)
+        c = w.to_int4().cuda()
+        try:
+            object.__setattr__(w, "_lbc_int4", c)
+        except (AttributeError, TypeError):
+            pass
+    return c
+
+
+def gemm_w4a8_amx(x, w, params: Params | None = None, isa=None, threads: int | None = None,
+                  _prep: _Prepared | None = None):
+    """lowbit's gemm_w4a8_amx (src/lowbit/kernels.py:208-217): W4A8 on weights in
+    the AMX repack layout (formats.AMXInt4Weights, or lowbit's own), fp32 X
+    quantized per token to int8 inside the call; the same results as
+    gemm_w4a8 on the unpacked weights (exact int32 group sums)."""
+    return gemm_w4a8(x, _amx_int4(w), params, isa, threads, _prep)
+
+
+def w4a8_group_acc_amx(a: Int8Acts, w):
+    """lowbit's w4a8_group_acc_amx (src/lowbit/kernels.py:220-225): exact int32
+    accumulators out[m, n, g] for AMX-packed weights."""
+    return w4a8_group_acc(a, _amx_int4(w))
 
 
 def _dev_acts(a: Int8Acts):

@@ -38,10 +38,40 @@ def load() -> C.CDLL:
     L.lb_gemm_w4a16.argtypes = [vp, i, i, vp, vp, vp, i, vp, pp]
     L.lb_gemm_mxfp4.argtypes = [vp, i, i, vp, vp, i, vp, pp]
     L.lb_gemm_w4a8.argtypes = [vp, i, i, vp, vp, vp, i, vp, pp]
-    for f in ("lb_gemm_w4a16", "lb_gemm_mxfp4", "lb_gemm_w4a8", "lb_active_isa", "lb_has_openmp",
-              "lb_max_threads", "lb_has_vnni"):
+    L.lb_gemm_w4a8_amx.argtypes = [vp, i, i, vp, vp, vp, i, vp, i]
+    for f in ("lb_gemm_w4a16", "lb_gemm_mxfp4", "lb_gemm_w4a8", "lb_gemm_w4a8_amx", "lb_active_isa",
+              "lb_has_openmp", "lb_max_threads", "lb_has_vnni", "lb_amx_available"):
         getattr(L, f).restype = C.c_int
     return L
+
+
+def amx_available() -> bool:
+    """The reference's own check (src/lowbit/kernels.py:89-94): AVX-512 active
+    and AMX-INT8 usable by this process."""
+    L = load()
+    return L.lb_active_isa() >= 2 and bool(L.lb_amx_available())
+
+
+class RefGemmAMX:
+    """One reference lb_gemm_w4a8_amx call (src/lowbit/csrc/kern_amx.c:121-164) on
+    host buffers, weights in the AMX repack layout (AMXInt4Weights: qw, scales,
+    sz = s * z)."""
+
+    def __init__(self, x: np.ndarray, wa, threads: int | None = None):
+        self.L = load()
+        self.x = np.ascontiguousarray(x, np.float32)
+        self.w = wa
+        self.m = self.x.shape[0]
+        self.y = np.empty((self.m, wa.n), np.float32)
+        self.threads = threads or os.cpu_count() or 1
+
+    def __call__(self) -> int:
+        w = self.w
+        rc = self.L.lb_gemm_w4a8_amx(_p(self.x), self.m, w.kp, _p(w.qw), _p(w.scales), _p(w.sz), w.n,
+                                     _p(self.y), self.threads)
+        if rc < 0:
+            raise ValueError(f"reference lb_gemm_w4a8_amx failed rc={rc}")
+        return rc
 
 
 def _p(a):

@@ -166,4 +166,8 @@ def main(ref_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    # the reference's `src` directory: argument, LOWBIT_REF_SRC, or a
+    # `reference` checkout beside this repository
+    import os
+    default = os.environ.get("LOWBIT_REF_SRC", str(HERE.parents[2] / "reference" / "src"))
+    main(sys.argv[1] if len(sys.argv) > 1 else default)
