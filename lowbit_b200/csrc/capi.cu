@@ -282,8 +282,11 @@ int plan_rows(int fmt, int M, int N, int Kp, const lbc_params *p, RowsPlan &P) {
   const int occ = rows_occupancy_cached(fmt, P.mt, P.ch, P.r, P.threads);
   if (occ <= 0) return fail(LBC_ERR_PARAMS, "decode kernel cannot be resident on an SM");
   // about 16 resident warps per SM by default: small-K rows (one-warp teams)
-  // need many CTAs per SM to keep enough loads in flight
-  P.cps = std::min((p && p->nb > 0) ? p->nb : std::max(4, 16 / nw), occ);
+  // need many CTAs per SM to keep enough loads in flight; W4A8 with one or
+  // two tokens (two chunks per thread, fewer registers) runs 8 (the tuner
+  // measured 1.10-1.40x over 4 on the BASELINE shapes)
+  const int cps_def = (fmt == lbc::FMT_W4A8 && M <= 2) ? 8 : std::max(4, 16 / nw);
+  P.cps = std::min((p && p->nb > 0) ? p->nb : cps_def, occ);
   // the kernel hands out whole blocks of r rows
   P.grid = std::max(1, std::min(ceil_div(N, P.r), di.sms * P.cps));
   return 0;

@@ -50,19 +50,28 @@ class Params:
     """Kernel tiling parameters (0 = library default), reinterpreted for the GPU:
 
     mr    tokens per pass of the SIMT kernels (1, 2, 4, 8)
-    nr    rows per team per pipeline tile (1 or 4)
+    nr    rows per team per pipeline tile (1 or 4); warps per CTA on the mma path
     nb    resident CTAs per SM
-    kb    split-K length in elements (multiple of 128), 0 = whole K
+    kb    split-K length in elements (multiple of 128), 0 = whole K; K elements
+          per ring stage on the mma path
     order TMA pipeline stages
+    isa   kernel path these parameters were tuned for ("simt", "tcgen05",
+          "mma"), used when the call gives no `isa`; None = automatic. The
+          reference's Params has no such field (its tuner searches one ISA);
+          the GPU tuner records the path it chose here.
     """
     mr: int = 0
     nr: int = 0
     nb: int = 0
     kb: int = 0
     order: int = 0
+    isa: str | None = None
 
     def as_dict(self) -> dict:
-        return asdict(self)
+        d = asdict(self)
+        if d["isa"] is None:
+            del d["isa"]
+        return d
 
 
 _vp = C.c_void_p
@@ -197,7 +206,7 @@ def _params(p, isa, kind=None, shape=None) -> _Params:
             raise ValueError(f"params must be a Params, None or 'auto', not {p!r}")
         p = auto_params(kind, *shape, isa=isa)
     p = p or Params()
-    return _Params(_path_id(isa), p.mr, p.nr, p.nb, p.kb, p.order, 0)
+    return _Params(_path_id(isa if isa is not None else p.isa), p.mr, p.nr, p.nb, p.kb, p.order, 0)
 
 
 def _pref(params, isa, kind: str, m: int, n: int, k: int):
