@@ -568,91 +568,186 @@ def _gemm_check(fmt: str, x: np.ndarray, W, y, plan: dict) -> float:
     return R.assert_close(ys, R.gemm_w4a8_ref(xq, xsc, asum, qw, sc, z), R.w4a8_bound(xq, xsc, asum, qw, sc, z), 1e-5)
 
 
+def _dist():
+    """(world, rank, device) of this process: torch.distributed over NCCL when
+    launched with WORLD_SIZE > 1 (one rank per GPU), else one GPU."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    return world, rank, dev
+
+
 def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int, reps: int = 10) -> dict:
     """One GEMM of `fmt` (w4a16 asym / w4a8 sym / mxfp4) on BASELINE's seeded
     inputs (numpy seeds 0 / 1, quantized on the GPU bit-identically to the
     reference's quantizers), device-resident, checked once against the
     oracle, then timed as a CUDA graph of `steps` calls over rotating weight
     copies (inputs + copies larger than L2), CUDA events, median of `reps`
-    replays."""
+    replays.
+
+    Under torch.distributed (WORLD_SIZE = P > 1, one rank per GPU) W is
+    column-sharded as BASELINE configs[3] asks: rank p keeps rows
+    shard_bounds(N, p, P) of the packed arrays, and a step is its slice's GEMM
+    plus the all-gather that assembles Y [M, N] on every rank (W4A16 with one
+    or two tokens: the GEMV with the all-gather fused in; otherwise NCCL
+    all_gather). The step time is the max over ranks; the oracle check runs on
+    rank 0's assembled Y; the GEMM alone and the gather's share are reported
+    beside it."""
     import torch
+    import torch.distributed as dist
     from lowbit_b200 import kernels as Kn
+    from lowbit_b200.formats import shard_bounds
     from lowbit_b200.kernels import quantize_int4_cuda, quantize_mxfp4_cuda
+    world, rank, dev = _dist()
     hbm, tf_burst, tf_sust, src = peaks()
     wh, xh = _gemm_inputs(m, n, k)
-    w = torch.from_numpy(wh).cuda()
-    x = torch.from_numpy(xh).cuda()
-    W = (quantize_mxfp4_cuda(w) if fmt == "mxfp4" else quantize_int4_cuda(w, asym=(fmt == "w4a16")))
+    w = torch.from_numpy(wh).to(dev)
+    x = torch.from_numpy(xh).to(dev)
+    Wfull = (quantize_mxfp4_cuda(w) if fmt == "mxfp4" else quantize_int4_cuda(w, asym=(fmt == "w4a16")))
     del w
-    wbytes = int(sum(t.numel() * t.element_size() for t in
-                     ((W.qw, W.e8m0) if fmt == "mxfp4" else (W.qw, W.scales, W.zeros)) if t is not None))
-    copies = int(max(1, min(16, np.ceil(2 * L2_BYTES / max(1, wbytes + 4 * m * (k + n))))))
+    fields = ("qw", "scales", "zeros", "e8m0")
     from dataclasses import replace
-    pool = [W] + [replace(W, **{f: getattr(W, f).clone() for f in ("qw", "scales", "zeros", "e8m0")
+    lo, hi = shard_bounds(n, rank, world)
+    W = Wfull if world == 1 else replace(Wfull, **{f: getattr(Wfull, f)[lo:hi].contiguous() for f in fields
+                                                   if getattr(Wfull, f, None) is not None})
+    n_loc = hi - lo
+    wbytes = int(sum(getattr(W, f).numel() * getattr(W, f).element_size() for f in fields
+                     if getattr(W, f, None) is not None))
+    copies = int(max(1, min(16, np.ceil(2 * L2_BYTES / max(1, wbytes + 4 * m * (k + n_loc))))))
+    pool = [W] + [replace(W, **{f: getattr(W, f).clone() for f in fields
                                 if getattr(W, f, None) is not None}) for _ in range(copies - 1)]
     fn = {"w4a16": Kn.gemm_w4a16, "w4a8": Kn.gemm_w4a8, "mxfp4": Kn.gemm_mxfp4}[fmt]
-    prep = Kn._Prepared(x, W.kp, n)
-    plan = Kn.describe_plan(fmt, m, n, W.kp)
-    fn(x, W, _prep=prep)
-    torch.cuda.synchronize()
-    parity = _gemm_check(fmt, xh, W, prep.y, plan)
-    for i in range(warmup):
+    prep = Kn._Prepared(x, W.kp, n_loc)
+    plan = Kn.describe_plan(fmt, m, n_loc, W.kp)
+    gather, fused = None, None
+    if world > 1:
+        from lowbit_b200.sharding import ColumnParallel, FusedColumnParallel
+        if fmt == "w4a16" and m <= 2:
+            fused = FusedColumnParallel(m, n)
+        else:
+            gather = ColumnParallel(m, n)
+
+    def gemm(i):
         fn(x, pool[i % copies], _prep=prep)
+
+    def step(i):
+        if fused is not None:
+            return fused(x, pool[i % copies], _prep=prep)
+        gemm(i)
+        return gather.gather(prep.y) if gather is not None else prep.y
+
+    y = step(0)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for i in range(steps):
-            fn(x, pool[i % copies], _prep=prep)
-    graph.replay()
+    parity = _gemm_check(fmt, xh, Wfull, y, plan) if rank == 0 else 0.0
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize()
-    ts = []
-    for _ in range(reps):
-        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
-        e0.record()
-        graph.replay()
-        e1.record()
+
+    def capture(f):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                for i in range(steps):
+                    f(i)
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()
         torch.cuda.synchronize()
-        ts.append(e0.elapsed_time(e1) * 1e3 / steps)
-    us = statistics.median(ts)
+        return g
+
+    def timed(g):
+        ts = []
+        for _ in range(reps):
+            if world > 1:
+                dist.barrier(device_ids=[dev.index])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3 / steps)
+        return statistics.median(ts)
+
+    g_step = capture(step)
+    t = [timed(g_step)]
+    if world > 1:
+        t.append(timed(capture(gemm)))
+        tt = torch.tensor(t, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = [float(v) for v in tt]
+    us = t[0]
     flops = 2.0 * m * n * k
-    byts = wbytes + 4 * m * W.kp + 4 * m * n
+    wbytes_all = wbytes if world == 1 else int(sum(getattr(Wfull, f).numel() * getattr(Wfull, f).element_size()
+                                                   for f in fields if getattr(Wfull, f, None) is not None))
+    byts = wbytes_all + 4 * m * W.kp + 4 * m * n
     peak_t = tf_burst * (2 if fmt == "w4a8" else 1)
-    tensor_bound = flops / (peak_t * 1e12) > byts / (hbm * 1e9)
-    ach = flops / us / 1e6 if tensor_bound else byts / us / 1e3
+    # the roofline of one rank's kernel: its FLOPs / bytes over its GEMM time
+    us_k = t[1] if world > 1 else us
+    f_loc, b_loc = 2.0 * m * n_loc * k, wbytes + 4 * m * W.kp + 4 * m * n_loc
+    tensor_bound = f_loc / (peak_t * 1e12) > b_loc / (hbm * 1e9)
+    ach = f_loc / us_k / 1e6 if tensor_bound else b_loc / us_k / 1e3
     peak = peak_t if tensor_bound else hbm
-    return {"fmt": fmt, "M": m, "N": n, "K": k, "us": round(us, 3), "TFLOP/s": round(flops / us / 1e6, 2),
+    line = {"fmt": fmt, "M": m, "N": n, "K": k, "us": round(us, 3), "TFLOP/s": round(flops / us / 1e6, 2),
             "GB/s": round(byts / us / 1e3, 1), "kernel": plan.get("kernel", plan.get("path")),
-            "parity": {"max_err_over_limit": round(parity, 4), "sample": "64 weight rows x 256 tokens, float64 oracle"},
+            "parity": {"max_err_over_limit": round(parity, 4), "sample": "64 weight rows x 256 tokens, float64 oracle"
+                       + (", rank 0's assembled Y" if world > 1 else "")},
             "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": round(ach, 2),
                          "peak": peak, "unit": "TFLOP/s" if tensor_bound else "GB/s", "frac": round(ach / peak, 4),
                          "peak_source": src + (" (int8: 2x the bf16 figure, assumed: not measured)"
                                                if tensor_bound and fmt == "w4a8" else "")},
             "weight_copies": copies}
+    if world > 1:
+        line["n_gpus"] = world
+        line["gemm_only_us"] = round(t[1], 3)
+        line["gather"] = ("fused into the GEMV (NVLink tagged-word stores)" if fused is not None
+                          else "NCCL all_gather of the [M, N/P] slices")
+        line["roofline"]["scope"] = "one rank's GEMM on its N/P rows"
+        if fused is not None:
+            fused.close()
+    del g_step
+    return line
 
 
-def run_gemm(args) -> dict:
+def run_gemm(args) -> dict | None:
     line = gemm_line(args.fmt, args.m, args.n, args.k, args.steps, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
     return {"metric": f"{args.fmt} GEMM time (M={args.m}, N={args.n}, K={args.k})", "value": line["us"],
-            "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": line["us"] / 1e3,
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": line["us"] / 1e3,
+            "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": {"w4a16": "f32 (bf16 from 64 tokens)", "w4a8": "int8/int32",
                       "mxfp4": "f32 (bf16 from 64 tokens)"}[args.fmt],
             "data": "synthetic: W ~ N(0,1) numpy default_rng(0), X ~ N(0,1) default_rng(1), quantized on the GPU "
                     "bit-identically to the reference's quantizers",
             "config": {"workload": f"{args.fmt} GEMM M={args.m} N={args.n} K={args.k}",
+                       "parallelism": f"N-shard x{world} + all-gather of Y" if world > 1 else "1 GPU",
                        "timing": "CUDA graph of `steps` calls over rotating weight copies, CUDA events, "
-                                 "median of 10 replays"},
+                                 "median of 10 replays" + (", max over ranks" if world > 1 else "")},
             "detail": line}
 
 
-def run_sweep(args) -> dict:
+def run_sweep(args) -> dict | None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     rows = []
     for fmt in ("w4a16", "w4a8", "mxfp4"):
         for m in SWEEP_M:
             for n, k in SWEEP_NK:
                 steps = max(3, min(args.steps, int(2e6 / (m * n * k / 1e6 + 50))))
                 rows.append(gemm_line(fmt, m, n, k, steps, 3))
-    return {"metric": "GEMM shape sweep (BASELINE configs[3], 1 GPU)", "rows": rows}
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    return {"metric": f"GEMM shape sweep (BASELINE configs[3], {world} GPU{'s' if world > 1 else ''})",
+            "n_gpus": world, "rows": rows}
 
 
 def run_tune(args) -> dict:
@@ -691,29 +786,43 @@ def run_model(args) -> dict:
     from oracle import model_ref as O
     from oracle import ref_lib
 
+    # tensor parallelism under torch.distributed.run: every linear column
+    # parallel over the ranks (one GPU each), the rest replicated
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
     cfg = PM.qwen2_0_5b_config()
     t_build = time.perf_counter()
     W = PM.random_weights(cfg, seed=0, scale=0.02)
-    m = PM.Model(cfg, W, backend="w4a16", asym=True)
+    m = PM.Model(cfg, W, backend="w4a16", asym=True, group=group)
     t_build = time.perf_counter() - t_build
     V, P, NEW = cfg.vocab_size, 128, 128
     prompt = np.random.default_rng(0).integers(0, V, P)
-    # the packed-weight file: write the quantized model, read it back
-    # (no quantization), check the logits are the same
-    import tempfile
-    with tempfile.TemporaryDirectory() as td:
-        pk = Path(td) / "model.safetensors"
-        t0 = time.perf_counter()
-        PM.save_packed(m, pk)
-        t_save = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        m_pk = PM.load_packed(pk)
-        torch.cuda.synchronize()
-        t_load = time.perf_counter() - t0
-        packed = {"bytes": pk.stat().st_size, "save_s": round(t_save, 2), "load_s": round(t_load, 2),
-                  "logits_identical": bool(np.array_equal(m_pk.forward(prompt[:16], logits="all"),
-                                                          m.forward(prompt[:16], logits="all")))}
-        del m_pk
+    packed = None
+    if world == 1:
+        # the packed-weight file: write the quantized model, read it back
+        # (no quantization), check the logits are the same
+        import tempfile
+        with tempfile.TemporaryDirectory() as td:
+            pk = Path(td) / "model.safetensors"
+            t0 = time.perf_counter()
+            PM.save_packed(m, pk)
+            t_save = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            m_pk = PM.load_packed(pk)
+            torch.cuda.synchronize()
+            t_load = time.perf_counter() - t0
+            packed = {"bytes": pk.stat().st_size, "save_s": round(t_save, 2), "load_s": round(t_load, 2),
+                      "logits_identical": bool(np.array_equal(m_pk.forward(prompt[:16], logits="all"),
+                                                              m.forward(prompt[:16], logits="all")))}
+            del m_pk
     prompts16 = np.random.default_rng(1).integers(0, V, (16, P))
     c1, c16 = m.new_cache(P + NEW), m.new_cache(P + NEW, batch=16)
     for _ in range(args.warmup):  # builds plans, workspaces and the decode graphs
@@ -747,24 +856,32 @@ def run_model(args) -> dict:
     def med(runs, key):
         return statistics.median(r[key] for r in runs)
 
-    dec1 = (NEW - 1) / med(runs1, "decode_s")
-    dec16 = 16 * (NEW - 1) / med(runs16, "decode_s")
-    line = {"metric": MODEL_METRIC, "value": round(dec1, 1), "unit": "tok/s", "n_gpus": 1,
+    d1, d16, p1, p16 = med(runs1, "decode_s"), med(runs16, "decode_s"), med(runs1, "prefill_s"), med(runs16, "prefill_s")
+    if world > 1:  # the slowest rank's times
+        tt = torch.tensor([d1, d16, p1, p16], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        d1, d16, p1, p16 = (float(v) for v in tt)
+    dec1 = (NEW - 1) / d1
+    dec16 = 16 * (NEW - 1) / d16
+    line = {"metric": MODEL_METRIC, "value": round(dec1, 1), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 / dec1, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: random_weights(seed 0, scale 0.02), prompt default_rng(0).integers(0, 151936, 128)",
             "config": {"workload": "Qwen2-0.5B-shaped decoder, w4a16 asym linears, prompt 128, 128 greedy tokens "
                                    "(BASELINE configs[4])", "layers": cfg.num_layers, "hidden": cfg.hidden_size,
                        "vocab": V, "prompt": P, "new_tokens": NEW,
+                       "parallelism": (f"tensor parallel x{world}: column-parallel linears + NCCL all-gather, "
+                                       "norms / RoPE / attention replicated" if world > 1 else "one GPU"),
                        "timing": "decode: 127 CUDA-graph replays of a whole decode step (host clock around "
-                                 "synchronised loops); a step = one token for every sequence of the batch"},
-            "prefill_tok_s": round(P / med(runs1, "prefill_s"), 1),
-            "batch16": {"decode_tok_s": round(dec16, 1), "prefill_tok_s": round(16 * P / med(runs16, "prefill_s"), 1),
-                        "ms_per_step": round(1e3 * med(runs16, "decode_s") / (NEW - 1), 4)},
+                                 "synchronised loops, max over ranks); a step = one token for every sequence "
+                                 "of the batch"},
+            "prefill_tok_s": round(P / p1, 1),
+            "batch16": {"decode_tok_s": round(dec16, 1), "prefill_tok_s": round(16 * P / p16, 1),
+                        "ms_per_step": round(1e3 * d16 / (NEW - 1), 4)},
             "build_s": round(t_build, 1), "packed_file": packed, "clocks": clocks}
     # parity and CPU baseline: the reference's computation on the host (its C
     # kernels for every linear), prefill then 3 teacher-forced decode steps
-    if ref_lib.available() and not args.no_cpu_baseline:
+    if ref_lib.available() and not args.no_cpu_baseline and world == 1:
         threads = os.cpu_count() or 1
         ocfg = O.Cfg(**{k: getattr(cfg, k) for k in O.Cfg.__dataclass_fields__})
         lin = {}
@@ -798,9 +915,16 @@ def run_model(args) -> dict:
                                           "lb_gemm_w4a16 for every linear (oracle/_ref) with the numpy glue, "
                                           "default tiles"}
     else:
-        why = "skipped (--no-cpu-baseline)" if args.no_cpu_baseline else \
-            "unavailable: oracle/_ref/liblowbit_ref.so not built"
+        why = ("skipped (--no-cpu-baseline)" if args.no_cpu_baseline else
+               "the one-GPU run reports it" if world > 1 else "unavailable: oracle/_ref/liblowbit_ref.so not built")
         line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": why}
+    if world > 1:
+        m.release_graphs()  # they hold NCCL calls
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank != 0:
+            return None
     return line
 
 
@@ -816,14 +940,21 @@ def main():
                     help="omit the secondary block (configs[1], configs[2], M=4096 prefill)")
     ap.add_argument("--workload", choices=["decode", "model", "gemm", "sweep", "tune"], default="decode")
     ap.add_argument("--fmt", choices=["w4a16", "w4a8", "mxfp4"], default="w4a16")
-    ap.add_argument("--m", type=int, default=4096)
-    ap.add_argument("--n", type=int, default=11008)
-    ap.add_argument("--k", type=int, default=4096)
+    # --M/--N/--K are the spellings torch.distributed.run passes through
+    # (it takes --m, --n, --k for abbreviations of its own options)
+    ap.add_argument("--m", "--M", dest="m", type=int, default=4096)
+    ap.add_argument("--n", "--N", dest="n", type=int, default=11008)
+    ap.add_argument("--k", "--K", dest="k", type=int, default=4096)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.workload in ("gemm", "sweep"):
-        print(json.dumps(run_gemm(args) if args.workload == "gemm" else run_sweep(args)), flush=True)
+        line = run_gemm(args) if args.workload == "gemm" else run_sweep(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
         return
     if args.workload == "tune":
         print(json.dumps(run_tune(args)), flush=True)
@@ -831,7 +962,9 @@ def main():
     if args.workload == "model":
         if args.steps > 50:
             args.steps = 3  # a step is a whole 128-token generation here
-        print(json.dumps(run_model(args)), flush=True)
+        line = run_model(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
         return
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:

@@ -90,6 +90,16 @@ const char *lbc_last_error(void);
 /* device status word of the current device: 0, or LBC_ERR_TIMEOUT after a
  * bounded device-side wait gave up; reset != 0 clears it. Synchronous. */
 int lbc_device_status(int reset);
+/* Limit of every bounded device-side wait (mbarrier phases, the tensor-core
+ * kernel's split-tile flags, the fused all-gather's arrivals) on the current
+ * device, in SM clock cycles, for kernels launched afterwards; <= 0 restores
+ * the default (4e9 cycles, about 2 s). A wait that runs out records
+ * LBC_ERR_TIMEOUT in lbc_device_status and its kernel returns. Synchronous.
+ * Returns 0 or LBC_ERR_CUDA. No reference counterpart (the reference has no
+ * device-side waits). */
+int lbc_set_wait_cycles(long long cycles);
+/* the current device's wait limit in clock cycles (the default when unset) */
+long long lbc_wait_cycles(void);
 
 /* Kernel configuration the planner picks for a GEMM of `kind` (0 w4a16,
  * 1 mxfp4, 2 w4a8) as a JSON object in buf; returns the path or an error.
@@ -202,24 +212,29 @@ int lbc_ipc_open_handle(const void *handle, void **dev_ptr);
 int lbc_ipc_close_handle(void *dev_ptr);
 
 /* W4A16 decode (M <= 2) of this rank's weight rows [row0, row0 + N_local) of
- * an N_total-row matrix, with the all-gather fused in. The call's epoch is
- * *epoch + 1 (`epoch`: this rank's zero-initialised device counter); every
- * output value is stored into y_peers[(epoch % 2) * world + p] for every rank
- * p (a DEVICE array of 2 * world pointers to [M, N_total] fp32 buffers: two
- * per rank, by call parity, peer pointers opened over IPC) at row0 + n; the
- * kernel then publishes the epoch in flag_peers[p][rank] for every p, waits
- * (bounded: LBC_ERR_TIMEOUT in lbc_device_status) until every rank's epoch
- * has arrived in flag_peers[rank][*], and stores it in *epoch. When the
- * stream's work completes, Y is whole on this GPU; nothing is baked into the
- * launch, so CUDA graphs of these calls replay correctly. `counter` is this
- * rank's zero-initialised CTA counter (one uint32). Returns LBC_PATH_SIMT or
- * a negative error (LBC_ERR_PARAMS for M > 2 or explicit tiling params). */
+ * an N_total-row matrix, with the all-gather fused in: when the stream's work
+ * completes, y (this rank's [M, N_total] fp32 output, device memory) holds
+ * every rank's rows. The call's epoch is *epoch + 1 (`epoch`: this rank's
+ * zero-initialised device counter). Each output value is written to this
+ * rank's rows of y and, as one 8-byte word (epoch << 32 | the value's fp32
+ * bits), into the landing buffer of every other rank at
+ * [epoch % 2][m][row0 + n]; land_peers is a DEVICE array of `world` pointers
+ * (this rank's own included, peers' opened over IPC) to zero-initialised
+ * landing buffers of LBC_GATHER_LAND_BYTES(N_total) bytes. The kernel then
+ * waits (bounded: LBC_ERR_TIMEOUT in lbc_device_status) until the other
+ * ranks' rows in its own landing buffer carry the epoch, copies them into y
+ * and stores the epoch in *epoch. The ranks' row ranges must tile
+ * [0, N_total). Nothing is baked into the launch, so CUDA graphs of these
+ * calls replay correctly. `counter` is this rank's zero-initialised CTA
+ * counter (one uint32). world <= LBC_GATHER_MAX_WORLD. Returns LBC_PATH_SIMT
+ * or a negative error (LBC_ERR_PARAMS for M > 2 or explicit tiling params). */
+#define LBC_GATHER_MAX_WORLD 8
+#define LBC_GATHER_LAND_BYTES(n_total) ((size_t)(n_total) * 2 * 2 * 8)
 int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw,
                              const float *scales, const uint8_t *zeros, int N_local,
-                             int row0, int N_total, float *const *y_peers,
-                             uint32_t *const *flag_peers, uint32_t *counter,
-                             uint32_t *epoch, int rank, int world, const lbc_params *p,
-                             void *stream);
+                             int row0, int N_total, float *y, uint64_t *const *land_peers,
+                             uint32_t *counter, uint32_t *epoch, int rank, int world,
+                             const lbc_params *p, void *stream);
 
 /* ---- on-device weight quantizers: bit-identical to the reference's numpy
  * quantizers (src/lowbit/formats.py:90-142 and :175-212), writing the packed

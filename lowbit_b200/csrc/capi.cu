@@ -17,8 +17,9 @@
 #include "kernels.h"
 
 namespace lbc {
-// device status word (see common.cuh); one per device, address passed to kernels
-__device__ int g_status = 0;
+// device status block (see common.cuh): int status, pad, int64 wait limit in
+// clock cycles (0 = default); one per device, address passed to kernels
+__device__ __align__(16) long long g_status_block[2] = {0, 0};
 }
 
 namespace {
@@ -54,7 +55,7 @@ DevInfo dev_info() {
     cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d);
     cudaDeviceGetAttribute(&di.smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, d);
     di.ok = (major == 10 && minor == 0);
-    if (di.ok && cudaGetSymbolAddress(reinterpret_cast<void **>(&di.status), lbc::g_status) != cudaSuccess) {
+    if (di.ok && cudaGetSymbolAddress(reinterpret_cast<void **>(&di.status), lbc::g_status_block) != cudaSuccess) {
       cudaGetLastError();
       di.status = nullptr;
     }
@@ -572,12 +573,24 @@ const char *lbc_last_error(void) { return g_err; }
 
 int lbc_device_status(int reset) {
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, lbc::g_status, sizeof(int)) != cudaSuccess) return LBC_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&v, lbc::g_status_block, sizeof(int)) != cudaSuccess) return LBC_ERR_CUDA;
   if (reset && v) {
     const int z = 0;
-    cudaMemcpyToSymbol(lbc::g_status, &z, sizeof(int));
+    cudaMemcpyToSymbol(lbc::g_status_block, &z, sizeof(int));
   }
   return v;
+}
+
+int lbc_set_wait_cycles(long long cycles) {
+  const long long v = cycles > 0 ? cycles : 0;
+  cudaError_t e = cudaMemcpyToSymbol(lbc::g_status_block, &v, sizeof v, sizeof(long long));
+  return e == cudaSuccess ? 0 : fail_cuda("cudaMemcpyToSymbol(wait limit)", e);
+}
+
+long long lbc_wait_cycles(void) {
+  long long v = 0;
+  if (cudaMemcpyFromSymbol(&v, lbc::g_status_block, sizeof v, sizeof(long long)) != cudaSuccess) return LBC_ERR_CUDA;
+  return v > 0 ? v : 4000000000LL;
 }
 
 int lbc_tc_selftest(int kind, int32_t *out, void *stream) {
@@ -882,24 +895,30 @@ int lbc_ipc_close_handle(void *dev_ptr) {
 }
 
 int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
-                             const uint8_t *zeros, int N_local, int row0, int N_total, float *const *y_peers,
-                             uint32_t *const *flag_peers, uint32_t *counter, uint32_t *epoch, int rank,
+                             const uint8_t *zeros, int N_local, int row0, int N_total, float *y,
+                             uint64_t *const *land_peers, uint32_t *counter, uint32_t *epoch, int rank,
                              int world, const lbc_params *p, void *stream) {
   if (int rc = check_shape(M, Kp, N_local, LBC_GROUP)) return rc;
-  if (!x || !qw || !scales || !y_peers || !flag_peers || !counter || !epoch || !al16(x) || !al16(qw))
+  if (!x || !qw || !scales || !y || !land_peers || !counter || !epoch || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer");
-  if (world < 1 || rank < 0 || rank >= world || row0 < 0 || row0 + N_local > N_total)
+  if (world < 1 || world > LBC_GATHER_MAX_WORLD || rank < 0 || rank >= world || row0 < 0 ||
+      row0 + N_local > N_total)
     return fail(LBC_ERR_SHAPE, "rank / world / row range out of bounds");
   if (!rows_eligible(lbc::FMT_W4A16, M, Kp, p))
     return fail(LBC_ERR_PARAMS, "the fused all-gather decode serves one or two tokens with default tiling");
   if (int rc = device_gate()) return rc;
   RowsPlan P;
   if (int rc = plan_rows(lbc::FMT_W4A16, M, N_local, Kp, p, P)) return rc;
+  // a CTA waits for peers' rows that other ranks' CTAs produce: every CTA of
+  // the grid must be resident at once
+  const int occ = lbc::rows_gather_occupancy(P.mt, P.ch, P.r, P.threads);
+  if (occ <= 0) return fail(LBC_ERR_PARAMS, "decode tile has no fused all-gather variant");
+  P.grid = std::min(P.grid, dev_info().sms * std::min(P.cps, occ));
   lbc::GemvArgs a{};
   a.x = x; a.qw = qw; a.scales = scales; a.zeros = zeros;
-  a.M = M; a.N = N_local; a.Kp = Kp;
+  a.M = M; a.N = N_local; a.Kp = Kp; a.y = y;
   a.status = dev_info().status;
-  a.y_peers = y_peers; a.flag_peers = flag_peers; a.counter = counter;
+  a.land_peers = land_peers; a.counter = counter;
   a.epoch = epoch; a.rank = rank; a.world = world; a.row0 = row0; a.ld_y = N_total;
   cudaError_t e = lbc::rows_gather_launch(a, P.mt, P.ch, P.r, dim3(P.grid, 1, 1), P.threads,
                                           static_cast<cudaStream_t>(stream));

@@ -1,7 +1,8 @@
 // Device helpers shared by the lowbit_b200 kernels (sm_100a only).
 //
-// Everything that waits on the GPU (mbarrier phases) is bounded: a wait gives
-// up after LBC_WAIT_CYCLES clock cycles, records LBC_ERR_TIMEOUT in the
+// Everything that waits on the GPU (mbarrier phases, flags) is bounded: a
+// wait gives up after the wait limit (LBC_WAIT_CYCLES clock cycles unless the
+// host set another with lbc_set_wait_cycles), records LBC_ERR_TIMEOUT in the
 // device status word and lets the caller return, so a logic error surfaces as
 // an error code instead of a hung GPU.
 #pragma once
@@ -17,13 +18,21 @@
 
 namespace lbc {
 
-// ~2 s at 2 GHz: far above any legitimate wait inside one GEMM launch.
+// Default limit of a bounded wait: ~2 s at 2 GHz, far above any legitimate
+// wait inside one GEMM launch.
 constexpr long long LBC_WAIT_CYCLES = 4000000000LL;
 
-// Device status word (0 = ok), passed to kernels by address. Written only on
-// a bounded-wait timeout; nullptr disables reporting.
+// Device status block, passed to kernels by the address of its first word:
+// word 0 = status (0 = ok; written only on a bounded-wait timeout), words 2-3 =
+// the wait limit in clock cycles (<= 0: the default), set by the host with
+// lbc_set_wait_cycles. nullptr disables reporting and uses the default limit.
 __device__ __forceinline__ void set_status(int *status, int code) {
   if (status) atomicExch(status, code);
+}
+__device__ __forceinline__ long long wait_cycles(const int *status) {
+  if (!status) return LBC_WAIT_CYCLES;
+  const long long v = *reinterpret_cast<const volatile long long *>(status + 2);
+  return v > 0 ? v : LBC_WAIT_CYCLES;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -102,15 +111,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity. Returns false (and sets
-// the device status) if the phase did not complete within LBC_WAIT_CYCLES.
+// the device status) if the phase did not complete within the wait limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status) {
   if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
+  const long long t0 = clock64(), lim = wait_cycles(status);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > LBC_WAIT_CYCLES) {
+    if (clock64() - t0 > lim) {
       set_status(status, LBC_ERR_TIMEOUT);
       return false;
     }

@@ -62,10 +62,11 @@ struct GemvArgs {
   int meta_tma;         // 1: scales/zeros/e8m0 travel with the weights in each stage
   int *status;          // device status word (bounded-wait timeouts)
   // fused all-gather (column-parallel decode over NVLink peers), else unused:
-  float *const *y_peers;        // [2][world] Y buffers [M, ld_y] of every rank, by call parity
-  uint32_t *const *flag_peers;  // [world] flag arrays [world] of every rank
+  // y is then this rank's whole output [M, ld_y]
+  uint64_t *const *land_peers;  // [world] landing buffers of every rank: [2 parities][2][ld_y]
+                                // words (call tag << 32 | fp32 bits of the value)
   uint32_t *counter;            // this rank's CTA completion counter
-  uint32_t *epoch;              // this rank's call counter (the flags carry it)
+  uint32_t *epoch;              // this rank's call counter (the words' tags carry it)
   int rank, world, row0, ld_y;  // this rank's first global row, Y row stride
   // fused activation prologue of the decode kernel (W4A16), else unused:
   const float *xres;  // [M, Kp] residual added to x before the norm, or nullptr

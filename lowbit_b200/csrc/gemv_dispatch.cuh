@@ -28,9 +28,11 @@ bool rows_combo(int mt, int ch, int r);
 cudaError_t rows_launch(int fmt, const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads,
                         cudaStream_t st);
 int rows_occupancy(int fmt, int mt, int ch, int r, int threads);
-// W4A16 decode with the column-parallel all-gather fused in (a.y_peers ...);
-// (mt, ch, r) in {(1,1,4), (1,2,4), (2,1,2)}
+// W4A16 decode with the column-parallel all-gather fused in (a.land_peers ...);
+// (mt, ch, r) in {(1,1,4), (1,2,4), (2,1,2)}; its resident CTAs per SM (0 when
+// not instantiated): every CTA of the launch must be resident at once
 cudaError_t rows_gather_launch(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads, cudaStream_t st);
+int rows_gather_occupancy(int mt, int ch, int r, int threads);
 // W4A16 decode with a fused activation prologue xm (XM_RMSNORM: a.xres, a.xout,
 // a.lnw, a.eps; XM_GLU: x rows of 2 * Kp), same combinations as rows_launch
 cudaError_t rows_fused_launch(const GemvArgs &a, int xm, int mt, int ch, int r, dim3 grid, int threads,

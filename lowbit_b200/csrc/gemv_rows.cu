@@ -59,10 +59,10 @@ cudaError_t rows_launch_one(const GemvArgs &a, dim3 grid, int threads, cudaStrea
   }
 }
 
-template <int FMT, int MT, int CH, int R, int NW>
+template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false>
 int rows_occ_nw() {
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_rows_kernel<FMT, MT, CH, R, NW>, NW * 32, 0) !=
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gemv_rows_kernel<FMT, MT, CH, R, NW, GATHER>, NW * 32, 0) !=
       cudaSuccess) {
     cudaGetLastError();
     return 0;
@@ -70,30 +70,30 @@ int rows_occ_nw() {
   return nb;
 }
 
-template <int FMT, int MT, int CH, int R>
+template <int FMT, int MT, int CH, int R, bool GATHER = false>
 int rows_occ_one(int threads) {
   if constexpr (CH == 1 && MT <= 2) {
     switch (threads / 32) {
-      case 9: return rows_occ_nw<FMT, MT, CH, R, 9>();
-      case 10: return rows_occ_nw<FMT, MT, CH, R, 10>();
-      case 11: return rows_occ_nw<FMT, MT, CH, R, 11>();
-      case 12: return rows_occ_nw<FMT, MT, CH, R, 12>();
-      case 13: return rows_occ_nw<FMT, MT, CH, R, 13>();
-      case 14: return rows_occ_nw<FMT, MT, CH, R, 14>();
-      case 15: return rows_occ_nw<FMT, MT, CH, R, 15>();
-      case 16: return rows_occ_nw<FMT, MT, CH, R, 16>();
+      case 9: return rows_occ_nw<FMT, MT, CH, R, 9, GATHER>();
+      case 10: return rows_occ_nw<FMT, MT, CH, R, 10, GATHER>();
+      case 11: return rows_occ_nw<FMT, MT, CH, R, 11, GATHER>();
+      case 12: return rows_occ_nw<FMT, MT, CH, R, 12, GATHER>();
+      case 13: return rows_occ_nw<FMT, MT, CH, R, 13, GATHER>();
+      case 14: return rows_occ_nw<FMT, MT, CH, R, 14, GATHER>();
+      case 15: return rows_occ_nw<FMT, MT, CH, R, 15, GATHER>();
+      case 16: return rows_occ_nw<FMT, MT, CH, R, 16, GATHER>();
       default: break;
     }
   }
   switch (threads / 32) {
-    case 1: return rows_occ_nw<FMT, MT, CH, R, 1>();
-    case 2: return rows_occ_nw<FMT, MT, CH, R, 2>();
-    case 3: return rows_occ_nw<FMT, MT, CH, R, 3>();
-    case 4: return rows_occ_nw<FMT, MT, CH, R, 4>();
-    case 5: return rows_occ_nw<FMT, MT, CH, R, 5>();
-    case 6: return rows_occ_nw<FMT, MT, CH, R, 6>();
-    case 7: return rows_occ_nw<FMT, MT, CH, R, 7>();
-    case 8: return rows_occ_nw<FMT, MT, CH, R, 8>();
+    case 1: return rows_occ_nw<FMT, MT, CH, R, 1, GATHER>();
+    case 2: return rows_occ_nw<FMT, MT, CH, R, 2, GATHER>();
+    case 3: return rows_occ_nw<FMT, MT, CH, R, 3, GATHER>();
+    case 4: return rows_occ_nw<FMT, MT, CH, R, 4, GATHER>();
+    case 5: return rows_occ_nw<FMT, MT, CH, R, 5, GATHER>();
+    case 6: return rows_occ_nw<FMT, MT, CH, R, 6, GATHER>();
+    case 7: return rows_occ_nw<FMT, MT, CH, R, 7, GATHER>();
+    case 8: return rows_occ_nw<FMT, MT, CH, R, 8, GATHER>();
     default: return 0;
   }
 }
@@ -119,6 +119,13 @@ cudaError_t rows_gather_launch_w4a16(const GemvArgs &a, int mt, int ch, int r, d
   return cudaErrorInvalidConfiguration;
 }
 
+int rows_gather_occ_w4a16(int mt, int ch, int r, int threads) {
+  if (mt == 1 && ch == 1 && r == 4) return rows_occ_one<FMT_W4A16, 1, 1, 4, true>(threads);
+  if (mt == 1 && ch == 2 && r == 4) return rows_occ_one<FMT_W4A16, 1, 2, 4, true>(threads);
+  if (mt == 2 && ch == 1 && r == 2) return rows_occ_one<FMT_W4A16, 2, 1, 2, true>(threads);
+  return 0;
+}
+
 template <int FMT>
 int rows_occ_fmt(int mt, int ch, int r, int threads) {
 #define LBC_ROWS_O(MT, CH, R) \
@@ -135,6 +142,10 @@ int rows_occ_fmt(int mt, int ch, int r, int threads) {
 
 cudaError_t rows_gather_launch(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads, cudaStream_t st) {
   return rows_gather_launch_w4a16(a, mt, ch, r, grid, threads, st);
+}
+
+int rows_gather_occupancy(int mt, int ch, int r, int threads) {
+  return rows_gather_occ_w4a16(mt, ch, r, threads);
 }
 
 bool rows_combo(int mt, int ch, int r) {

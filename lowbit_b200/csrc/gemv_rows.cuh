@@ -49,31 +49,37 @@ __device__ __forceinline__ float4 glu4(float4 g, float4 u) {
   return make_float4(glu1(g.x, u.x), glu1(g.y, u.y), glu1(g.z, u.z), glu1(g.w, u.w));
 }
 
-__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t *p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// 8-byte words that carry their own call tag: a single-copy-atomic store is
+// seen by a peer either whole or not at all, so no fence orders data and flag
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
   uint32_t old;
   asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // GATHER: column-parallel decode with the all-gather fused in. The call's
 // epoch is the device counter + 1 (read after griddepcontrol.wait, so a
-// launch that starts early under PDL sees the previous call's update); each
-// output value goes to this rank's rows of its epoch-parity Y buffer; the
-// last CTA to finish copies the slice into every peer's buffer (peer pointers
-// over NVLink), publishes the epoch in every rank's flag array, waits
-// (bounded) until every rank's epoch has arrived in its own, and advances the
-// counter. When the kernel
-// completes, Y is whole on this GPU. No epoch is baked into the launch, so a
-// CUDA graph of these calls replays correctly.
+// launch that starts early under PDL sees the previous call's update). Each
+// output value goes to this rank's own Y rows and, as one 8-byte word
+// (epoch << 32 | fp32 bits), into every peer's landing buffer (peer pointers
+// over NVLink) at the epoch's parity; the stores leave as the rows finish,
+// overlapping the rest of the GEMV. Then every CTA polls its share of the
+// global rows in its own landing buffer (bounded) until each word carries
+// this epoch and copies the values into Y. The word is its own flag: no
+// fence, arrival counter or last-CTA copy sits between the GEMV and the
+// exchange. Every CTA of the grid is resident at once (the host sizes the
+// grid by occupancy), so a CTA's wait on a peer's row never blocks the CTA
+// that produces it. The CTA completing the grid advances the call counter.
+// When the kernel completes, Y is whole on this GPU; no epoch is baked into
+// the launch, so a CUDA graph of these calls replays correctly.
 template <int FMT, int MT, int CH, int R, int NW, bool GATHER = false, int XM = XM_PLAIN>
 __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   static_assert(XM == XM_PLAIN || FMT == FMT_W4A16, "fused prologues are W4A16 only");
@@ -138,9 +144,15 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
     }
   };
 
+  // landing buffers of every rank (static across calls), from shared memory
+  __shared__ uint64_t *land[GATHER ? LBC_GATHER_MAX_WORLD : 1];
+  if (GATHER && tid < a.world) land[tid] = a.land_peers[tid];
+  (void)land;
+
   // weights are static: the first block streams before the previous kernel
   // (which may produce X) has finished
   if (nblk > 0) load(0, 0);
+  if (GATHER) __syncthreads();  // land[] is read by other threads
   pdl_launch_dependents();
   pdl_wait_prior_grid();
 
@@ -260,12 +272,12 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   for (int t = 0; t < MT; ++t) xsc[t] = (FMT == FMT_W4A8 && m0 + t < a.M) ? ld_act(a.xs + m0 + t) : 1.f;
   const uint32_t MAG = opaque(0x4B000000u);
   uint32_t epoch = 0;
-  float *const *ydst = nullptr;
+  size_t land_off = 0;  // the epoch parity's half of every landing buffer
   if (GATHER) {
     epoch = *reinterpret_cast<volatile const uint32_t *>(a.epoch) + 1u;
-    ydst = a.y_peers + (epoch & 1u) * a.world;
+    land_off = (size_t)(epoch & 1u) * 2 * a.ld_y;
   }
-  (void)ydst;
+  (void)land_off;
 
   auto compute = [&](int b, int buf) {
     float part[R][MT];
@@ -339,7 +351,11 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
       if (rr < nrows && m < a.M) {
         const float out = (FMT == FMT_W4A8) ? val * xsc[t] : val;
         if (GATHER) {
-          ydst[a.rank][(size_t)m * a.ld_y + a.row0 + r_begin + rr] = out;  // local slice first
+          const size_t at = (size_t)m * a.ld_y + a.row0 + r_begin + rr;
+          a.y[at] = out;
+          const uint64_t word = ((uint64_t)epoch << 32) | __float_as_uint(out);
+          for (int p = 0; p < a.world; ++p)
+            if (p != a.rank) st_relaxed_sys_u64(land[p] + land_off + at, word);
         } else {
           a.y[(size_t)m * a.N + r_begin + rr] = out;
         }
@@ -357,53 +373,36 @@ __global__ void __launch_bounds__(NW * 32) gemv_rows_kernel(const GemvArgs a) {
   }
 
   if (GATHER) {
-    __shared__ int last;
-    // the CTA's slice rows are released (bar.sync, then thread 0's release
-    // atomic, cumulative over the CTA) before it counts itself; the CTA that
-    // completes the count acquires every slice, copies the whole slice to
-    // every peer with 16-byte stores (one coalesced stream per peer), then
-    // one system-scope fence orders the copies before the epoch flags
-    __syncthreads();
-    if (tid == 0) {
-      const uint32_t total = gridDim.x * gridDim.y;
-      last = (atom_add_acq_rel_gpu(a.counter, 1u) + 1u == total) ? 1 : 0;
-      if (last) atomicExch(a.counter, 0u);  // ready for the next call
-    }
-    __syncthreads();
-    if (!last) return;
-    const int nloc = a.N;
-    for (int p = 0; p < a.world; ++p) {
-      if (p == a.rank) continue;
-      for (int m = 0; m < a.M; ++m) {
-        const float *src = ydst[a.rank] + (size_t)m * a.ld_y + a.row0;
-        float *dst = ydst[p] + (size_t)m * a.ld_y + a.row0;
-        // scalar head up to 16-byte alignment, vector body, scalar tail
-        const int head = min(nloc, (int)((16 - (reinterpret_cast<uintptr_t>(src) & 15)) & 15) / 4);
-        for (int j = tid; j < head; j += NT) dst[j] = src[j];
-        const int nvec = (nloc - head) / 4;
-        const float4 *s4 = reinterpret_cast<const float4 *>(src + head);
-        float4 *d4 = reinterpret_cast<float4 *>(dst + head);
-        for (int j = tid; j < nvec; j += NT) d4[j] = s4[j];
-        for (int j = head + 4 * nvec + tid; j < nloc; j += NT) dst[j] = src[j];
-      }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      fence_acq_rel_sys();
-      for (int p = 0; p < a.world; ++p) st_relaxed_sys_u32(a.flag_peers[p] + a.rank, epoch);
-      // flags only grow: a rank already at a later call has also passed this one
-      const uint32_t *mine = a.flag_peers[a.rank];
-      const long long t0 = clock64();
-      for (int p = 0; p < a.world; ++p) {
-        while ((int32_t)(ld_acquire_sys_u32(mine + p) - epoch) < 0) {
-          if (clock64() - t0 > LBC_WAIT_CYCLES) {
-            set_status(a.status, LBC_ERR_TIMEOUT);
-            return;
-          }
-          __nanosleep(32);
+    // this CTA's share of the global rows (any split works: every CTA is
+    // resident); this rank's own rows are already in Y
+    const int g0 = (int)((long long)blockIdx.x * a.ld_y / gridDim.x);
+    const int g1 = (int)((long long)(blockIdx.x + 1) * a.ld_y / gridDim.x);
+    const int span = g1 - g0;
+    const uint64_t *mine = land[a.rank] + land_off;
+    const long long t0 = clock64(), lim = wait_cycles(a.status);
+    bool gave_up = false;
+    for (int e = tid; e < a.M * span && !gave_up; e += NT) {
+      const int m = e / span, row = g0 + e % span;
+      if (row >= a.row0 && row < a.row0 + a.N) continue;
+      const size_t at = (size_t)m * a.ld_y + row;
+      uint64_t v = ld_relaxed_sys_u64(mine + at);
+      while ((uint32_t)(v >> 32) != epoch) {
+        if (clock64() - t0 > lim) {
+          set_status(a.status, LBC_ERR_TIMEOUT);
+          gave_up = true;
+          break;
         }
+        v = ld_relaxed_sys_u64(mine + at);
       }
-      *a.epoch = epoch;
+      if (!gave_up) a.y[at] = __uint_as_float((uint32_t)v);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      // every CTA read the epoch before counting itself (acq_rel atomic)
+      if (atom_add_acq_rel_gpu(a.counter, 1u) + 1u == gridDim.x * gridDim.y) {
+        atomicExch(a.counter, 0u);  // ready for the next call
+        *a.epoch = epoch;
+      }
     }
   }
 }

@@ -566,11 +566,11 @@ __global__ void __maxnreg__(80) tcgemm_kernel(const __grid_constant__ CUtensorMa
           if (row == 0) {
             const uint32_t *f = a.flags + (size_t)chunk * NCTA + c;
             bool seen = ld_acquire_u32(f) == a.epoch;
-            const long long t0 = clock64();
+            const long long t0 = clock64(), lim = wait_cycles(a.status);
             while (!seen) {
               __nanosleep(128);
               seen = ld_acquire_u32(f) == a.epoch;
-              if (!seen && clock64() - t0 > LBC_WAIT_CYCLES) {
+              if (!seen && clock64() - t0 > lim) {
                 set_status(a.status, LBC_ERR_TIMEOUT);
                 *abort_flag = 1;
                 break;

@@ -90,6 +90,8 @@ def lib() -> C.CDLL:
         "lbc_sm_count": ([], _int),
         "lbc_last_error": ([], C.c_char_p),
         "lbc_device_status": ([_int], _int),
+        "lbc_set_wait_cycles": ([C.c_longlong], _int),
+        "lbc_wait_cycles": ([], C.c_longlong),
         "lbc_describe_plan": ([_int, _int, _int, _int, _pp, C.c_char_p, _int], _int),
         "lbc_tc_selftest": ([_int, _vp, _vp], _int),
         "lbc_gemm_w4a16": ([_vp, _int, _int, _vp, _vp, _vp, _int, _vp, _pp, _vp], _int),
@@ -529,6 +531,16 @@ def tc_selftest(kind: int):
     out = torch.full((128, 16), -12345, dtype=torch.int32, device="cuda")
     _check(lib().lbc_tc_selftest(kind, out.data_ptr(), _stream()), "lbc_tc_selftest")
     return out.cpu().numpy()
+
+
+def set_wait_cycles(cycles: int) -> None:
+    """Limit of every bounded device-side wait on the current device, in SM
+    clock cycles (<= 0: the default, about 2 s); for kernels launched afterwards."""
+    _check(lib().lbc_set_wait_cycles(int(cycles)), "lbc_set_wait_cycles")
+
+
+def wait_cycles() -> int:
+    return int(lib().lbc_wait_cycles())
 
 
 def device_status(reset: bool = True) -> int:

@@ -255,6 +255,66 @@ class _LowbitLinear(Linear):
         return C.byref(_params(self.params, None, self.kind, (m, self.wq.n, self.wq.k)))
 
 
+class ColumnParallelLinear(Linear):
+    """Tensor parallelism for one linear (column parallel, as the north star and
+    the survey fix it): this rank's rows shard_bounds(N, rank, world) of W in
+    `inner` (any backend), Y [M, N] assembled on every rank, then the full
+    bias. W4A16 decode (one or two tokens, default tiling) runs the GEMV with
+    the all-gather fused in (lowbit_b200.sharding.FusedColumnParallel, one per
+    (tokens, N) shared by the model's linears of that width); everything else
+    runs the slice's GEMM and an NCCL all-gather (sharding.ColumnParallel).
+    The model replicates the rest (norms, RoPE, attention: 14 query / 2 KV
+    heads do not divide by 4 or 8)."""
+
+    def __init__(self, inner: Linear, n: int, b, group, fused_pool: dict | None = None):
+        from ._torch import to_cuda
+        from .formats import shard_bounds
+        import torch.distributed as dist
+        self.inner, self.n, self.k, self.group = inner, n, inner.k, group
+        self.kind = inner.kind
+        self.b = None if b is None else to_cuda(np.asarray(b, np.float32))
+        self.threads = inner.threads
+        self.nbytes = inner.nbytes
+        self.lo, self.hi = shard_bounds(n, dist.get_rank(group), dist.get_world_size(group))
+        self._cps: dict = {}
+        self._fused = fused_pool
+
+    @property
+    def wq(self):
+        return self.inner.wq
+
+    @property
+    def params(self):
+        return getattr(self.inner, "params", None)
+
+    @params.setter
+    def params(self, p):
+        self.inner.params = p
+
+    def mm(self, x):
+        from .sharding import ColumnParallel, FusedColumnParallel
+        m = int(x.shape[0])
+        if (self._fused is not None and m <= 2 and self.kind == "w4a16" and self.params is None
+                and self.inner.wq.kp % 128 == 0):
+            fc = self._fused.get((m, self.n))
+            if fc is None:
+                fc = self._fused[(m, self.n)] = FusedColumnParallel(m, self.n, self.group)
+            return fc(self.inner._x(x), self.inner.d)
+        y = self.inner.mm(x)
+        cp = self._cps.get(m)
+        if cp is None:
+            cp = self._cps[m] = ColumnParallel(m, self.n, self.group)
+        return cp.gather(y)
+
+
+def tp_shard(w: np.ndarray, rank: int, world: int) -> np.ndarray:
+    """Rows shard_bounds(N, rank, world) of a weight [N, K]: this rank's part of
+    a column-parallel linear."""
+    from .formats import shard_bounds
+    lo, hi = shard_bounds(w.shape[0], rank, world)
+    return np.ascontiguousarray(w[lo:hi])
+
+
 class W4A16Linear(_LowbitLinear):
     kind = "w4a16"
 
@@ -396,7 +456,7 @@ class Model:
 
     def __init__(self, cfg: ModelConfig, weights: dict, backend: str = "fp32", threads: int | None = None,
                  asym: bool = False, quantize_lm_head: bool = True, params=None, int4_scale: str = "absmax",
-                 _packed: tuple | None = None):
+                 _packed: tuple | None = None, group=None):
         from ._torch import require_cuda, to_cuda
         require_cuda()
         if backend not in LINEARS:
@@ -410,11 +470,27 @@ class Model:
         def g(n):
             return np.asarray(W[n], np.float32)
 
+        # tensor parallelism over `group` (a torch.distributed process group,
+        # one rank per GPU): every linear column parallel, the rest replicated
+        tp_world, tp_rank = 1, 0
+        if group is not None:
+            import torch.distributed as dist
+            tp_world, tp_rank = dist.get_world_size(group), dist.get_rank(group)
+        self.group, self.tp_world, self.tp_rank = group, tp_world, tp_rank
+        self._tp_fused: dict = {}   # fused all-gather decode state per (tokens, N)
+
         def linear(name, cls, w, b):
             """The linear `name`: quantized from fp32 (w(), b() give the
-            arrays), or built from a packed file's arrays (load_packed)."""
+            arrays), or built from a packed file's arrays (load_packed); with
+            tensor parallelism this rank's row shard plus the all-gather."""
             if _packed is None:
+                if tp_world > 1:
+                    wf = w()
+                    inner = cls(tp_shard(wf, tp_rank, tp_world), None, **kw)
+                    return ColumnParallelLinear(inner, wf.shape[0], b(), group, self._tp_fused)
                 return cls(w(), b(), **kw)
+            if tp_world > 1:
+                raise ValueError("tensor parallelism builds from fp32 weights, not packed files")
             return _packed_linear(name, cls, _packed, kw)
 
         self.embed = to_cuda(np.ascontiguousarray(g("model.embed_tokens.weight")))
@@ -453,7 +529,7 @@ class Model:
         self.cos, self.sin = to_cuda(cos), to_cuda(sin)
         # decode steps fuse the norms and the SiLU*up into the w4a16 GEMVs
         # (default tiling, unpadded hidden and intermediate sizes)
-        self._fusable = (backend == "w4a16" and params is None and cfg.hidden_size % 128 == 0
+        self._fusable = (backend == "w4a16" and params is None and tp_world == 1 and cfg.hidden_size % 128 == 0
                          and cfg.intermediate_size % 128 == 0)
         self._graphs: dict = {}
 
@@ -588,6 +664,15 @@ class Model:
         torch.cuda.current_stream().wait_stream(s)
         self._graphs = {"decode": (cache, g, tok)}  # one live decode graph per model
         return g, tok
+
+    def release_graphs(self) -> None:
+        """Drop the cached decode graph (with tensor parallelism it holds NCCL
+        calls: release it before destroying the process group) and close the
+        fused all-gather buffers (collective: every rank calls it)."""
+        self._graphs = {}
+        for fc in self._tp_fused.values():
+            fc.close()
+        self._tp_fused.clear()
 
     def _step(self, tok, cache: KVCache):
         torch = _torch()

@@ -68,17 +68,19 @@ def gemm_sharded(kind: str, x, w_local, cp: ColumnParallel, **kw):
 
 class FusedColumnParallel:
     """W4A16 decode (one or two tokens) with the all-gather fused into the
-    kernel: every rank's GEMV stores its Y rows straight into the Y buffer of
-    every rank over NVLink (CUDA IPC peer pointers) and signals completion
-    with a per-call epoch flag, so no separate collective runs.
+    kernel (``lbc_gemm_w4a16_allgather``): every rank's GEMV writes its own Y
+    rows and sends each value to every other rank over NVLink (CUDA IPC peer
+    pointers) as one 8-byte word tagged with the call's epoch; each rank's
+    CTAs wait for the words of this epoch in its own landing buffer and copy
+    them into its Y. No separate collective runs and no fence or flag sits
+    between the GEMV and the exchange.
 
-    Y is double-buffered by call parity: a rank may start call e + 2 only
-    after every rank finished call e + 1, and a rank's call e + 1 reads its X
-    only after whatever consumed Y(e) on that GPU, so no store lands in a
-    buffer still being read. The call counter lives on the device (CUDA-graph
-    replays stay correct); ``__call__`` returns a view of the Y buffer of the
-    call it launched, by the host's own count of calls, so read it only when
-    every call went through ``__call__`` (not a graph replay).
+    The landing buffers alternate halves by call parity: a rank writes call
+    e + 2 into a peer's buffer only after its own call e + 1 received that
+    peer's call e + 1 rows, which that peer produced after its call e ended.
+    The call counter lives on the device (CUDA-graph replays stay correct).
+    ``__call__`` returns this rank's Y, alternating between two buffers by the
+    host's count of calls, so the previous call's result stays readable.
     """
 
     def __init__(self, m: int, n: int, group=None):
@@ -92,10 +94,11 @@ class FusedColumnParallel:
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the fused all-gather decode serves at most 8 ranks")
         self.m, self.n = m, n
         self.lo, self.hi = shard_bounds(n, self.rank, self.world)
         L = K.lib()
-        ybytes = 2 * m * n * 4
         self._own = []
 
         def alloc(nbytes):
@@ -104,59 +107,42 @@ class FusedColumnParallel:
             self._own.append(p.value)
             return p.value
 
-        self._y = alloc(ybytes)
-        self._flags = alloc(4 * self.world)
-        self._counter = alloc(256)  # byte 0: CTA counter, byte 128: call epoch
-        handles = []
-        for ptr in (self._y, self._flags):
-            h = (C.c_char * 64)()
-            K._check(L.lbc_ipc_get_handle(ptr, h), "lbc_ipc_get_handle")
-            handles.append(bytes(h))
+        self._land = alloc(n * 2 * 2 * 8)   # LBC_GATHER_LAND_BYTES(n)
+        self._counter = alloc(256)          # byte 0: CTA counter, byte 128: call epoch
+        h = (C.c_char * 64)()
+        K._check(L.lbc_ipc_get_handle(self._land, h), "lbc_ipc_get_handle")
         everyone = [None] * self.world
-        dist.all_gather_object(everyone, handles, group=group)
+        dist.all_gather_object(everyone, bytes(h), group=group)
         self._opened = []
-        ys, fs = [], []
-        for r, (hy, hf) in enumerate(everyone):
+        lands = []
+        for r, hr in enumerate(everyone):
             if r == self.rank:
-                ys.append(self._y)
-                fs.append(self._flags)
+                lands.append(self._land)
                 continue
-            for h, out in ((hy, ys), (hf, fs)):
-                p = C.c_void_p()
-                buf = (C.c_char * 64).from_buffer_copy(h)
-                K._check(L.lbc_ipc_open_handle(buf, C.byref(p)), "lbc_ipc_open_handle")
-                self._opened.append(p.value)
-                out.append(p.value)
+            p = C.c_void_p()
+            buf = (C.c_char * 64).from_buffer_copy(hr)
+            K._check(L.lbc_ipc_open_handle(buf, C.byref(p)), "lbc_ipc_open_handle")
+            self._opened.append(p.value)
+            lands.append(p.value)
         dev = torch.cuda.current_device()
-        half = m * n * 4
-        self._yptrs = torch.tensor([y + par * half for par in (0, 1) for y in ys], dtype=torch.int64, device=dev)
-        self._fptrs = torch.tensor(fs, dtype=torch.int64, device=dev)
+        self._lptrs = torch.tensor(lands, dtype=torch.int64, device=dev)
+        self._ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(2)]
         self.epoch = 0
-        self._yview = [self._as_tensor(self._y + par * half, (m, n)) for par in (0, 1)]
         dist.barrier(group=group)
-
-    def _as_tensor(self, ptr, shape):
-        """A float32 CUDA tensor aliasing library-owned device memory."""
-        torch = self.torch
-
-        class _Arr:
-            __cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 3,
-                                        "strides": None}
-        return torch.as_tensor(_Arr(), device="cuda")
 
     def __call__(self, x, w_local, params=None, _prep=None):
         K, C = self.K, self.C
         self.epoch += 1
-        par = self.epoch & 1
+        y = self._ys[self.epoch & 1]
         pr = _prep or K._Prepared(x, w_local.kp, w_local.n)
         d = K._dev_weights(w_local)
         rc = K.lib().lbc_gemm_w4a16_allgather(
             pr.x.data_ptr(), pr.m, w_local.kp, d.qw.data_ptr(), d.scales.data_ptr(),
             None if d.zeros is None else d.zeros.data_ptr(), w_local.n, self.lo, self.n,
-            self._yptrs.data_ptr(), self._fptrs.data_ptr(), self._counter, self._counter + 128,
+            y.data_ptr(), self._lptrs.data_ptr(), self._counter, self._counter + 128,
             self.rank, self.world, C.byref(K._params(params, None)), K._stream())
         K._check(rc, "lbc_gemm_w4a16_allgather")
-        return self._yview[par]
+        return y
 
     def resync(self):
         """Re-read the device call counter (after CUDA-graph replays of these calls)."""
@@ -180,6 +166,8 @@ class FusedColumnParallel:
         for p in self._opened:
             L.lbc_ipc_close_handle(p)
         self._opened = []
+        # no peer maps this rank's landing buffer any more once all have closed
+        self.torch.distributed.barrier(group=self.group)
         for p in self._own:
             L.lbc_device_free(p)
         self._own = []

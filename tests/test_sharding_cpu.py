@@ -70,3 +70,44 @@ def test_padded_rows():
     assert padded_rows(11008, 8) == 1376
     assert padded_rows(37, 2) == 19
     assert [lb.formats.shard_bounds(37, r, 2) for r in range(2)] == [(0, 19), (19, 37)]
+
+
+def _tp_shard_rank(rank, world, port, q):
+    import os
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from lowbit_b200.model import tp_shard
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = np.random.default_rng(5).standard_normal((151936 // 64, 24)).astype(np.float32)
+        part = torch.from_numpy(tp_shard(w, rank, world))
+        parts = [None] * world
+        dist.all_gather_object(parts, part)
+        q.put((rank, bool(np.array_equal(torch.cat(parts).numpy(), w))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_shards_reassemble_the_weight_gloo():
+    """Tensor-parallel model: every rank's column-parallel shard of a weight
+    (tp_shard) concatenated in rank order is the whole weight (gloo, world 2)."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_shard_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] and res[1]
