@@ -628,20 +628,24 @@ def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int, reps: i
     plan = Kn.describe_plan(fmt, m, n_loc, W.kp)
     gather, fused = None, None
     if world > 1:
-        from lowbit_b200.sharding import ColumnParallel, FusedColumnParallel
+        from lowbit_b200.sharding import ColumnParallel, FusedColumnParallel, FusedColumnParallelGemm
+        gather = ColumnParallel(m, n)          # NCCL all-gather (timed beside)
         if fmt == "w4a16" and m <= 2:
             fused = FusedColumnParallel(m, n)
-        else:
-            gather = ColumnParallel(m, n)
+        elif plan.get("kernel") == "prefill":
+            fused = FusedColumnParallelGemm(fmt, m, n)
 
     def gemm(i):
         fn(x, pool[i % copies], _prep=prep)
 
+    def step_nccl(i):
+        gemm(i)
+        return gather.gather(prep.y) if gather is not None else prep.y
+
     def step(i):
         if fused is not None:
             return fused(x, pool[i % copies], _prep=prep)
-        gemm(i)
-        return gather.gather(prep.y) if gather is not None else prep.y
+        return step_nccl(i)
 
     y = step(0)
     torch.cuda.synchronize()
@@ -681,6 +685,7 @@ def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int, reps: i
     t = [timed(g_step)]
     if world > 1:
         t.append(timed(capture(gemm)))
+        t.append(timed(capture(step_nccl)) if fused is not None else t[0])
         tt = torch.tensor(t, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t = [float(v) for v in tt]
@@ -708,8 +713,10 @@ def gemm_line(fmt: str, m: int, n: int, k: int, steps: int, warmup: int, reps: i
     if world > 1:
         line["n_gpus"] = world
         line["gemm_only_us"] = round(t[1], 3)
-        line["gather"] = ("fused into the GEMV (NVLink tagged-word stores)" if fused is not None
-                          else "NCCL all_gather of the [M, N/P] slices")
+        line["nccl_step_us"] = round(t[2], 3)
+        line["gather"] = ("fused into the GEMV (NVLink tagged-word stores)" if fused is not None and m <= 2
+                          else "fused into the prefill GEMM's store (NVLink peer stores per output tile)"
+                          if fused is not None else "NCCL all_gather of the [M, N/P] slices")
         line["roofline"]["scope"] = "one rank's GEMM on its N/P rows"
         if fused is not None:
             fused.close()
@@ -853,6 +860,25 @@ def run_model(args) -> dict:
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
 
+    # per-section device time (Model.prof, the reference's linear / attention /
+    # lm_head / other split) of one profiled generation, untimed: the prompt's
+    # prefill, then the graph-replayed decode steps (event-record nodes at the
+    # section boundaries: a profiled step is slower than the timed ones)
+    m.prof.enabled = True
+    m.prof.reset()
+    c1.reset()
+    tp = {}
+    m.generate(prompt, NEW, cache=c1, timings=tp)
+    m.prof.enabled = False
+    m.prof.reset()
+    steps_d = NEW - 1
+    profile = {"unit": "us",
+               "prefill_128": {k: round(v * 1e6, 1) for k, v in sorted(tp["prof_prefill"].items())},
+               "decode_per_step": {k: round(v * 1e6 / steps_d, 2) for k, v in sorted(tp["prof_decode"].items())},
+               "decode_step_wall_us_profiled": round(tp["decode_s"] * 1e6 / steps_d, 2),
+               "note": "device time from each section boundary to the next (CUDA events); fused decode GEMVs "
+                       "(input norm, SiLU*up inside) count as linear"}
+
     def med(runs, key):
         return statistics.median(r[key] for r in runs)
 
@@ -878,7 +904,7 @@ def run_model(args) -> dict:
             "prefill_tok_s": round(P / p1, 1),
             "batch16": {"decode_tok_s": round(dec16, 1), "prefill_tok_s": round(16 * P / p16, 1),
                         "ms_per_step": round(1e3 * d16 / (NEW - 1), 4)},
-            "build_s": round(t_build, 1), "packed_file": packed, "clocks": clocks}
+            "build_s": round(t_build, 1), "packed_file": packed, "clocks": clocks, "profile_b1": profile}
     # parity and CPU baseline: the reference's computation on the host (its C
     # kernels for every linear), prefill then 3 teacher-forced decode steps
     if ref_lib.available() and not args.no_cpu_baseline and world == 1:

@@ -236,6 +236,28 @@ int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw,
                              uint32_t *counter, uint32_t *epoch, int rank, int world,
                              const lbc_params *p, void *stream);
 
+/* Many-token GEMM (M >= 64: the tcgen05 prefill kernel; kind 0 w4a16, 1
+ * mxfp4, 2 w4a8, arguments as lbc_gemm_w4a16 / _mxfp4 / _w4a8) of this
+ * rank's weight rows [row0, row0 + N_local) of an N_total-row matrix, with
+ * the all-gather fused into the GEMM's store: every finished output tile is
+ * written to every rank's Y buffer y_peers[(epoch % 2) * world + p] (a DEVICE
+ * array of 2 * world pointers to [M, N_total] fp32 buffers, two per rank by
+ * call parity, peers' opened over IPC) at row0 + n, over NVLink while later
+ * tiles are computed. The call's epoch is *epoch + 1; when this rank's CTAs
+ * are done, its last CTA adds one to flag_peers[p][rank] for every p
+ * (zero-initialised uint32 call counters, [world] per rank), waits (bounded:
+ * LBC_ERR_TIMEOUT in lbc_device_status) until flag_peers[rank][q] has
+ * reached the epoch for every q and stores the epoch in *epoch. When the
+ * stream's work completes, Y of the call's parity is whole on this GPU;
+ * CUDA graphs of these calls replay correctly. `counter` is this rank's
+ * zero-initialised CTA counter. Returns LBC_PATH_TCGEN05 or a negative
+ * error (LBC_ERR_PARAMS below 64 tokens or with explicit tiling). */
+int lbc_gemm_allgather(int kind, const float *x, int M, int Kp, const uint8_t *qw,
+                       const float *scales, const uint8_t *zeros, const uint8_t *e8m0,
+                       int N_local, int row0, int N_total, float *const *y_peers,
+                       uint32_t *const *flag_peers, uint32_t *counter, uint32_t *epoch,
+                       int rank, int world, const lbc_params *p, void *stream);
+
 /* ---- on-device weight quantizers: bit-identical to the reference's numpy
  * quantizers (src/lowbit/formats.py:90-142 and :175-212), writing the packed
  * layouts above from a row-major fp32 W [N, K] in device memory (Kp = K

@@ -927,6 +927,54 @@ int lbc_gemm_w4a16_allgather(const float *x, int M, int Kp, const uint8_t *qw, c
   return LBC_PATH_SIMT;
 }
 
+int lbc_gemm_allgather(int kind, const float *x, int M, int Kp, const uint8_t *qw, const float *scales,
+                       const uint8_t *zeros, const uint8_t *e8m0, int N_local, int row0, int N_total,
+                       float *const *y_peers, uint32_t *const *flag_peers, uint32_t *counter, uint32_t *epoch,
+                       int rank, int world, const lbc_params *p, void *stream) {
+  const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : kind == 2 ? lbc::FMT_W4A8 : -1;
+  if (fmt < 0) return fail(LBC_ERR_SHAPE, "kind must be 0 (w4a16), 1 (mxfp4) or 2 (w4a8)");
+  if (int rc = check_shape(M, Kp, N_local, fmt == lbc::FMT_MXFP4 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
+  if (!x || !qw || !y_peers || !flag_peers || !counter || !epoch || !al16(x) || !al16(qw) ||
+      (fmt == lbc::FMT_MXFP4 ? !e8m0 : !scales))
+    return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer");
+  if (world < 1 || rank < 0 || rank >= world || row0 < 0 || row0 + N_local > N_total)
+    return fail(LBC_ERR_SHAPE, "rank / world / row range out of bounds");
+  if (!want_prefill(p, fmt, M) || (p && p->isa >= 0 && p->isa != LBC_PATH_TCGEN05))
+    return fail(LBC_ERR_PARAMS, "the fused all-gather GEMM runs the prefill kernel: 64+ tokens, default tiling "
+                                "(one or two tokens: lbc_gemm_w4a16_allgather)");
+  if (int rc = device_gate()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  lbc::TcCall c{};
+  c.fmt = fmt; c.x = x; c.qw = qw; c.scales = scales; c.zeros = zeros; c.e8m0 = e8m0;
+  c.M = M; c.N = N_local; c.Kp = Kp; c.prefill = 1;
+  c.y_peers = y_peers; c.flag_peers = flag_peers; c.counter = counter; c.epoch = epoch;
+  c.rank = rank; c.world = world; c.row0 = row0; c.ld_y = N_total;
+  if (fmt != lbc::FMT_W4A8) return run_tc(c, st);
+  // W4A8: the per-token int8 activations first, in a stream-ordered workspace
+  size_t off_xs, off_as, off_tc;
+  const size_t bytes = w4a8_ws_layout(M, Kp, &off_xs, &off_as, &off_tc);
+  void *tmp = nullptr;
+  if (cudaMallocAsync(&tmp, bytes, st) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(LBC_ERR_ALLOC, "cudaMallocAsync(workspace) failed");
+  }
+  uint8_t *ws = static_cast<uint8_t *>(tmp);
+  int8_t *xq = reinterpret_cast<int8_t *>(ws);
+  float *xs = reinterpret_cast<float *>(ws + off_xs);
+  int32_t *asum = reinterpret_cast<int32_t *>(ws + off_as);
+  int rc = 0;
+  cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, st);
+  if (e != cudaSuccess) rc = fail_cuda("quant_act_int8 launch", e);
+  if (rc == 0) {
+    c.x = nullptr; c.xq = xq; c.xs = xs; c.asum = asum;
+    c.scratch = ws + off_tc;
+    c.scratch_bytes = bytes - off_tc;
+    rc = run_tc(c, st);
+  }
+  cudaFreeAsync(ws, st);
+  return rc;
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------------ host buffers

@@ -59,11 +59,6 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // GATHER: column-parallel decode with the all-gather fused in. The call's
 // epoch is the device counter + 1 (read after griddepcontrol.wait, so a

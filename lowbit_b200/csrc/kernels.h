@@ -48,6 +48,11 @@ struct TcCall {
   int *status;
   int sms, smem_optin;
   int prefill;             // 1: 128-token prefill kernel (bf16 W4A16 / MXFP4: 4e-3 tolerance; W4A8 exact), 0: exact kernel
+  // prefill only: the all-gather fused into the store (TcArgs), else nullptr
+  float *const *y_peers;
+  uint32_t *const *flag_peers;
+  uint32_t *counter, *epoch;
+  int rank, world, row0, ld_y;
 };
 // scratch for format `fmt` (FMT_* id), M tokens, Kp columns when the grid
 // has `ctas` CTAs (at most the SM count)

@@ -148,7 +148,15 @@ int tc_prefill(const TcCall &c, cudaStream_t st, char *err, size_t errlen) {
   // at 64-512 tokens): every split keeps at least one 256-K unit
   // (at most one item per SM, so no CTA runs two)
   a.ksplit = 1;
-  if (2 * a.units <= c.sms) a.ksplit = std::min(a.nkb, c.sms / a.units);
+  if (2 * a.units <= c.sms && !c.y_peers) a.ksplit = std::min(a.nkb, c.sms / a.units);
+  a.y_peers = c.y_peers;  // fused all-gather (never split: the store is the exchange)
+  a.flag_peers = c.flag_peers;
+  a.ag_counter = c.counter;
+  a.ag_epoch = c.epoch;
+  a.rank = c.rank;
+  a.world = c.world;
+  a.row0 = c.row0;
+  a.ld_y = c.ld_y;
   const int items = a.units * a.ksplit;
   const int grid_x = items < c.sms ? items : c.sms;
   CUtensorMap map;

@@ -76,6 +76,14 @@ struct TcArgs {
   int b_block_bytes;     // bytes of one activation block in shared memory
   int ksplit;            // prefill: K ranges per output tile (>= 1; > 1 adds into a zeroed Y)
   int *status;
+  // prefill with the column-parallel all-gather fused into the store (ksplit
+  // 1), else y_peers is nullptr: this rank's rows [row0, row0 + N) of every
+  // output go to every rank's Y buffer of the call's parity
+  float *const *y_peers;         // [2][world] Y buffers [M, ld_y] of every rank, by call parity
+  uint32_t *const *flag_peers;   // [world] call counters of every rank: flag_peers[p][q] = calls of q seen by p
+  uint32_t *ag_counter;          // this rank's CTA counter
+  uint32_t *ag_epoch;            // this rank's call counter
+  int rank, world, row0, ld_y;
 };
 
 __host__ __device__ constexpr int tc_nmma(int mt, int npiece) {

@@ -90,9 +90,10 @@ cudaError_t tc_prefill_launch(const CUtensorMap &map, const TcArgs &a, int nch, 
                                st, a.x, a.xq, const_cast<uint8_t *>(a.bglob), a.M, a.Kp, a.nkb, a.b_block_bytes);
     if (e != cudaSuccess) return e;
   }
-  auto k = a.ksplit > 1 ? tcprefill_kernel<FMT, true> : tcprefill_kernel<FMT, false>;
-  static int enabled[2][64] = {{0}};
-  const int sk = a.ksplit > 1 ? 1 : 0;
+  auto k = a.y_peers ? tcprefill_kernel<FMT, false, true>
+                     : a.ksplit > 1 ? tcprefill_kernel<FMT, true> : tcprefill_kernel<FMT, false>;
+  static int enabled[3][64] = {{0}};
+  const int sk = a.y_peers ? 2 : a.ksplit > 1 ? 1 : 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && enabled[sk][dev] < smem) {

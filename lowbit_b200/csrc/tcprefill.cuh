@@ -29,7 +29,12 @@
 //     15 warps leave 128 registers per thread on B200's four sub-partitions;
 //     where
 //     several warps wait for the same event, one polls the mbarrier and the
-//     others wait on a named barrier, blocked in hardware.
+//     others wait on a named barrier, blocked in hardware;
+//   * column parallelism (a.y_peers): each rank owns rows [row0, row0 + N) of
+//     an ld_y-row weight; the epilogue stores every finished tile into every
+//     rank's Y over NVLink (peer pointers) while later tiles are still being
+//     computed, so the all-gather overlaps the GEMM; a per-call counter per
+//     rank tells each GPU when all rows have arrived.
 #pragma once
 
 #include "tcgemm.cuh"
@@ -40,8 +45,9 @@ constexpr int PF_TOK = 128;     // tokens per tile (MMA N)
 constexpr int PF_THREADS = 480;  // 4 dequantising + producer + 2 MMA + 8 epilogue warps
 
 // SPLIT: the split-K instantiation (a.ksplit > 1); without it the K range of
-// an item is the whole row and the position bookkeeping folds away
-template <int FMT, bool SPLIT>
+// an item is the whole row and the position bookkeeping folds away. GATHER:
+// the column-parallel instantiation (a.y_peers, never split).
+template <int FMT, bool SPLIT, bool GATHER = false>
 __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtensorMap wmap, const TcArgs a) {
   constexpr bool I8 = (FMT == FMT_W4A8);
   constexpr int NMMA = PF_TOK;
@@ -342,6 +348,12 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
     const int row = 32 * q + lane;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     pdl_wait_prior_grid();  // Y may still be read by the previous kernel
+    // fused all-gather: this call's parity of every rank's Y buffers
+    float *const *ydst = nullptr;
+    if (GATHER) {
+      const uint32_t ep = *reinterpret_cast<volatile const uint32_t *>(a.ag_epoch) + 1u;
+      ydst = a.y_peers + (ep & 1u) * a.world;
+    }
     auto load_scales = [&](Pos p, float (&sc)[2]) {
       const int n = (p.t / nch) * TC_ROWS + row;
 #pragma unroll
@@ -415,6 +427,27 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
 #pragma unroll
             for (int j = 0; j < ECOLS; ++j) slot[(size_t)j * TC_ROWS] = yacc[j];
           }
+        } else if (GATHER) {
+          // fused all-gather: the tile's values go to every rank's Y at
+          // global row row0 + n (own buffer first, then the peers in rank
+          // order from the next one, so the ranks' stores spread over the
+          // links); each store instruction is 128 contiguous bytes
+          if (ok && n < a.N) {
+            if (I8) {
+#pragma unroll
+              for (int j = 0; j < ECOLS; ++j)
+                if (j < mlim) yacc[j] *= ld_act(a.xs + m0 + j);
+            }
+            for (int i = 0; i < a.world; ++i) {
+              const int pr = (a.rank + i < a.world) ? a.rank + i : a.rank + i - a.world;
+              float *yp = ydst[pr] + (size_t)m0 * a.ld_y + a.row0 + n;
+#pragma unroll
+              for (int j = 0; j < ECOLS; ++j) {
+                if (j < mlim) *yp = yacc[j];
+                yp += a.ld_y;
+              }
+            }
+          }
         } else if (ok && n < a.N) {
           float *yp = a.y + (size_t)m0 * a.N + n;
 #pragma unroll
@@ -435,6 +468,35 @@ __global__ void __maxnreg__(128) tcprefill_kernel(const __grid_constant__ CUtens
   if (warp == W_MMA) {
     tc::fence_after_sync();
     tc::dealloc(tmem, 512);
+  }
+  // fused all-gather: every thread's stores precede the barrier above; one
+  // system-scope fence orders them before this CTA counts itself. The CTA
+  // completing this rank's grid adds one call to every rank's counter for
+  // this rank, waits (bounded) until every rank has counted this call in
+  // this rank's counters, and advances the call counter. Counters only grow,
+  // so a rank already at a later call has also passed this one.
+  if (GATHER && tid == 0) {
+    const uint32_t ep = *reinterpret_cast<volatile const uint32_t *>(a.ag_epoch) + 1u;
+    fence_acq_rel_sys();
+    if (atom_add_acq_rel_gpu(a.ag_counter, 1u) + 1u == gridDim.x) {
+      atomicExch(a.ag_counter, 0u);  // ready for the next call
+      fence_acq_rel_sys();
+      for (int p = 0; p < a.world; ++p) red_add_relaxed_sys_u32(a.flag_peers[p] + a.rank, 1u);
+      const uint32_t *mine = a.flag_peers[a.rank];
+      const long long t0 = clock64(), lim = wait_cycles(a.status);
+      bool gave_up = false;
+      for (int p = 0; p < a.world && !gave_up; ++p) {
+        while ((int32_t)(ld_acquire_sys_u32(mine + p) - ep) < 0) {
+          if (clock64() - t0 > lim) {
+            set_status(a.status, LBC_ERR_TIMEOUT);
+            gave_up = true;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      *a.ag_epoch = ep;
+    }
   }
 }
 

@@ -111,6 +111,8 @@ def lib() -> C.CDLL:
         "lbc_ipc_close_handle": ([_vp], _int),
         "lbc_gemm_w4a16_allgather": ([_vp, _int, _int, _vp, _vp, _vp, _int, _int, _int, _vp, _vp, _vp, _vp,
                                       _int, _int, _pp, _vp], _int),
+        "lbc_gemm_allgather": ([_int, _vp, _int, _int, _vp, _vp, _vp, _vp, _int, _int, _int, _vp, _vp, _vp, _vp,
+                                _int, _int, _pp, _vp], _int),
         "lbc_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _int, _int, C.c_float, _vp], _int),
         "lbc_qkv_rope": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _int, _vp], _int),
         "lbc_attention": ([_vp, _vp, _vp, _vp, _vp, _int, _int, _int, _int, _int, _int, _vp], _int),

@@ -26,6 +26,8 @@ from __future__ import annotations
 
 import json
 import time
+from collections import defaultdict
+from contextlib import contextmanager
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -165,6 +167,90 @@ def load_safetensors(path: Path | str) -> dict[str, np.ndarray]:
         arr = (raw.astype(np.uint32) << 16).view(np.float32) if dt == "BF16" else raw.astype(np.float32)
         out[name] = arr.reshape(info["shape"])
     return out
+
+
+# ---------------------------------------------------------------- profile
+
+class Profile:
+    """Device time per section, accumulated across forward calls: the GPU
+    counterpart of the reference's Profile (src/lowbit/model.py:243-261), with
+    the same `t`, `enabled`, `section(name)` and `reset()` and the sections it
+    uses (linear, attention, lm_head, other). One CUDA timing event is
+    recorded on the current stream where a section begins; the time from it
+    to the next boundary (the next section, or the end of the forward) is the
+    section's device time. Reading `t` synchronises and folds pending events
+    in. Inside a CUDA-graph capture the events become event-record nodes of
+    the graph, kept with it and read after each replay, so graph-replayed
+    decode steps are split on the device's own clock. Event nodes sit between
+    the kernels and cost each boundary the overlap of consecutive launches:
+    a profiled step runs slower than an unprofiled one. The fused decode
+    kernels count as "linear" (the input norms and SiLU*up run inside the
+    GEMVs there). Off by default."""
+
+    def __init__(self, enabled: bool = False):
+        self.enabled = enabled
+        self._t: dict = defaultdict(float)
+        self._pending: list = []
+        self._sink: list | None = None
+        self._open = None  # (name, start event) of the section in progress
+
+    def _mark(self):
+        e = _torch().cuda.Event(enable_timing=True, external=True)
+        e.record()
+        if self._open is not None:
+            name, e0 = self._open
+            (self._sink if self._sink is not None else self._pending).append((name, e0, e))
+        return e
+
+    @contextmanager
+    def section(self, name: str):
+        if not self.enabled:
+            yield
+            return
+        if self._open is None or self._open[0] != name:
+            self._open = (name, self._mark())
+        yield
+
+    def close(self) -> None:
+        """End the section in progress (at the end of a forward)."""
+        if self.enabled and self._open is not None:
+            self._mark()
+            self._open = None
+
+    @contextmanager
+    def capturing(self):
+        """Collect the sections recorded inside a graph capture (returned list)
+        instead of treating them as pending."""
+        marks: list = []
+        self.close()
+        prev, self._sink = self._sink, marks
+        try:
+            yield marks
+        finally:
+            self.close()
+            self._sink = prev
+
+    def add(self, marks) -> None:
+        """Fold the (synchronised) events of one graph replay into the totals."""
+        for name, e0, e1 in marks:
+            self._t[name] += e0.elapsed_time(e1) * 1e-3
+
+    def collect(self) -> None:
+        self.close()
+        if self._pending:
+            _torch().cuda.synchronize()
+            self.add(self._pending)
+            self._pending = []
+
+    @property
+    def t(self) -> dict:
+        self.collect()
+        return self._t
+
+    def reset(self) -> None:
+        self._t = defaultdict(float)
+        self._pending = []
+        self._open = None
 
 
 # ---------------------------------------------------------------- linear backends
@@ -532,6 +618,7 @@ class Model:
         self._fusable = (backend == "w4a16" and params is None and tp_world == 1 and cfg.hidden_size % 128 == 0
                          and cfg.intermediate_size % 128 == 0)
         self._graphs: dict = {}
+        self.prof = Profile()
 
     # ------------------------------------------------------------ bookkeeping
 
@@ -564,7 +651,9 @@ class Model:
         n = B * T
         eps = float(cfg.rms_norm_eps)
         S = cache.capacity
-        x = self.embed.index_select(0, tok)
+        P = self.prof
+        with P.section("other"):
+            x = self.embed.index_select(0, tok)
         h = torch.empty((n, hid), dtype=torch.float32, device=x.device)
         q = torch.empty((n, H * D), dtype=torch.float32, device=x.device)
         att = torch.empty((n, H * D), dtype=torch.float32, device=x.device)
@@ -577,44 +666,58 @@ class Model:
         res = None
         for li, L in enumerate(self.layers):
             if fuse:
-                qkv = L.qkv.mm_rmsnorm(x, res, xb, L.ln1, eps)
+                with P.section("linear"):
+                    qkv = L.qkv.mm_rmsnorm(x, res, xb, L.ln1, eps)
                 if res is not None:
                     x, xb = xb, x
             else:
-                _check(lib.lbc_rmsnorm(x.data_ptr(), None if res is None else res.data_ptr(), x.data_ptr(),
-                                       L.ln1.data_ptr(), h.data_ptr(), n, hid, eps, st), "lbc_rmsnorm")
-                qkv = L.qkv.mm(h)
+                with P.section("other"):
+                    _check(lib.lbc_rmsnorm(x.data_ptr(), None if res is None else res.data_ptr(), x.data_ptr(),
+                                           L.ln1.data_ptr(), h.data_ptr(), n, hid, eps, st), "lbc_rmsnorm")
+                with P.section("linear"):
+                    qkv = L.qkv.mm(h)
             bias = None if L.qkv.b is None else L.qkv.b.data_ptr()
-            if T == 1:  # one launch: RoPE, cache append and attention
-                _check(lib.lbc_rope_attention(qkv.data_ptr(), bias, self.cos.data_ptr(), self.sin.data_ptr(),
-                                              cache.pos.data_ptr(), cache.k[li].data_ptr(), cache.v[li].data_ptr(),
-                                              att.data_ptr(), B, H, KV, D, S, st), "lbc_rope_attention")
-            else:
-                _check(lib.lbc_qkv_rope(qkv.data_ptr(), bias, self.cos.data_ptr(), self.sin.data_ptr(),
-                                        cache.pos.data_ptr(), q.data_ptr(), cache.k[li].data_ptr(),
-                                        cache.v[li].data_ptr(), B, T, H, KV, D, S, st), "lbc_qkv_rope")
-                _check(lib.lbc_attention(q.data_ptr(), cache.k[li].data_ptr(), cache.v[li].data_ptr(),
-                                         cache.pos.data_ptr(), att.data_ptr(), B, T, H, KV, D, S, st),
-                       "lbc_attention")
-            y = L.o.mm(att)
+            with P.section("attention"):
+                if T == 1:  # one launch: RoPE, cache append and attention
+                    _check(lib.lbc_rope_attention(qkv.data_ptr(), bias, self.cos.data_ptr(), self.sin.data_ptr(),
+                                                  cache.pos.data_ptr(), cache.k[li].data_ptr(),
+                                                  cache.v[li].data_ptr(), att.data_ptr(), B, H, KV, D, S, st),
+                           "lbc_rope_attention")
+                else:
+                    _check(lib.lbc_qkv_rope(qkv.data_ptr(), bias, self.cos.data_ptr(), self.sin.data_ptr(),
+                                            cache.pos.data_ptr(), q.data_ptr(), cache.k[li].data_ptr(),
+                                            cache.v[li].data_ptr(), B, T, H, KV, D, S, st), "lbc_qkv_rope")
+                    _check(lib.lbc_attention(q.data_ptr(), cache.k[li].data_ptr(), cache.v[li].data_ptr(),
+                                             cache.pos.data_ptr(), att.data_ptr(), B, T, H, KV, D, S, st),
+                           "lbc_attention")
+            with P.section("linear"):
+                y = L.o.mm(att)
             if fuse:
-                gu = L.gate_up.mm_rmsnorm(x, y, xb, L.ln2, eps)
+                with P.section("linear"):
+                    gu = L.gate_up.mm_rmsnorm(x, y, xb, L.ln2, eps)
                 x, xb = xb, x
-                res = L.down.mm_glu(gu)
+                with P.section("linear"):
+                    res = L.down.mm_glu(gu)
             else:
-                _check(lib.lbc_rmsnorm(x.data_ptr(), y.data_ptr(), x.data_ptr(), L.ln2.data_ptr(), h.data_ptr(),
-                                       n, hid, eps, st), "lbc_rmsnorm")
-                gu = L.gate_up.mm(h)
-                _check(lib.lbc_silu_mul(gu.data_ptr(), m.data_ptr(), n, I, st), "lbc_silu_mul")
-                res = L.down.mm(m)
-        xn = torch.empty_like(h)
-        _check(lib.lbc_rmsnorm(x.data_ptr(), res.data_ptr(), x.data_ptr(), self.norm.data_ptr(), xn.data_ptr(),
-                               n, hid, eps, st), "lbc_rmsnorm")
+                with P.section("other"):
+                    _check(lib.lbc_rmsnorm(x.data_ptr(), y.data_ptr(), x.data_ptr(), L.ln2.data_ptr(),
+                                           h.data_ptr(), n, hid, eps, st), "lbc_rmsnorm")
+                with P.section("linear"):
+                    gu = L.gate_up.mm(h)
+                with P.section("other"):
+                    _check(lib.lbc_silu_mul(gu.data_ptr(), m.data_ptr(), n, I, st), "lbc_silu_mul")
+                with P.section("linear"):
+                    res = L.down.mm(m)
+        with P.section("other"):
+            xn = torch.empty_like(h)
+            _check(lib.lbc_rmsnorm(x.data_ptr(), res.data_ptr(), x.data_ptr(), self.norm.data_ptr(), xn.data_ptr(),
+                                   n, hid, eps, st), "lbc_rmsnorm")
         if logits == "none":
             return xn
-        if logits == "last":
-            return self.lm_head(xn.view(B, T, hid)[:, T - 1].contiguous())
-        return torch.cat([self.lm_head(xn[i:i + head_chunk]) for i in range(0, n, head_chunk)])
+        with P.section("lm_head"):
+            if logits == "last":
+                return self.lm_head(xn.view(B, T, hid)[:, T - 1].contiguous())
+            return torch.cat([self.lm_head(xn[i:i + head_chunk]) for i in range(0, n, head_chunk)])
 
     def forward(self, tokens, cache: KVCache | None = None, logits: str = "last",
                 head_chunk: int = 256) -> np.ndarray:
@@ -632,6 +735,7 @@ class Model:
             raise ValueError(f"KV cache full ({cache.length}+{T} > {cache.capacity})")
         tok = torch.from_numpy(tokens).to("cuda")
         out = self._run(tok, 1, T, cache, logits, head_chunk)
+        self.prof.close()
         cache.length = cache.length + T
         out = out.cpu().numpy()
         return out[0] if logits == "last" else out
@@ -643,7 +747,7 @@ class Model:
         in `tok`, run every layer at cache.pos, argmax into `tok`, pos += 1."""
         torch = _torch()
         live = self._graphs.get("decode")
-        if live is not None and live[0] is cache:
+        if live is not None and live[0] is cache and live[3] == self.prof.enabled:
             return live[1], live[2]
         B = cache.batch
         tok = torch.zeros(B, dtype=torch.int64, device="cuda")
@@ -659,10 +763,14 @@ class Model:
             self._step(tok, cache)
             cache.pos.fill_(saved)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
-            self._step(tok, cache)
+        self.prof.collect()  # the warm-up step's sections, before the capture
+        with self.prof.capturing() as marks:
+            with torch.cuda.graph(g, stream=s):
+                self._step(tok, cache)
         torch.cuda.current_stream().wait_stream(s)
-        self._graphs = {"decode": (cache, g, tok)}  # one live decode graph per model
+        # one live decode graph per model; with profiling on it records the
+        # sections of every replay (marks)
+        self._graphs = {"decode": (cache, g, tok, self.prof.enabled, marks)}
         return g, tok
 
     def release_graphs(self) -> None:
@@ -677,8 +785,10 @@ class Model:
     def _step(self, tok, cache: KVCache):
         torch = _torch()
         logit = self._run(tok, cache.batch, 1, cache, "last")
-        tok.copy_(torch.argmax(logit, dim=-1))
-        _check(_lib().lbc_advance_pos(cache.pos.data_ptr(), 1, _stream()), "lbc_advance_pos")
+        with self.prof.section("other"):
+            tok.copy_(torch.argmax(logit, dim=-1))
+            _check(_lib().lbc_advance_pos(cache.pos.data_ptr(), 1, _stream()), "lbc_advance_pos")
+        self.prof.close()
 
     def generate(self, prompt, n_new: int, cache: KVCache | None = None, timings: dict | None = None,
                  graph: bool = True) -> list[int]:
@@ -707,16 +817,23 @@ class Model:
         logit = self._run(torch.from_numpy(prompts.reshape(-1)).to("cuda"), B, T0, cache, "last")
         cache.length = cache.length + T0
         if n_new > 0:
-            hist[0].copy_(torch.argmax(logit, dim=-1))
+            with self.prof.section("other"):
+                hist[0].copy_(torch.argmax(logit, dim=-1))
+        self.prof.close()
         torch.cuda.synchronize()
         t1 = time.perf_counter()
+        prof0 = dict(self.prof.t) if self.prof.enabled else None
         if n_new > 1:
             if graph:
                 g, tok = self._decode_graph(cache)
+                marks = self._graphs["decode"][4] if self.prof.enabled else None
                 tok.copy_(hist[0])
                 for i in range(1, n_new):
                     g.replay()
                     hist[i].copy_(tok)
+                    if marks:  # read this replay's section events
+                        torch.cuda.synchronize()
+                        self.prof.add(marks)
             else:
                 tok = hist[0].clone()
                 for i in range(1, n_new):
@@ -729,6 +846,10 @@ class Model:
             timings["prefill_s"] = t1 - t0
             timings["decode_s"] = t2 - t1
             timings["decode_forwards"] = max(0, n_new - 1)
+            if prof0 is not None:  # the section split of this call (reference e2e.py:_one_run)
+                now = self.prof.t
+                timings["prof_prefill"] = {k: v for k, v in prof0.items()}
+                timings["prof_decode"] = {k: now[k] - prof0.get(k, 0.0) for k in now}
         return out
 
 

@@ -148,16 +148,7 @@ class FusedColumnParallel:
         """Re-read the device call counter (after CUDA-graph replays of these calls)."""
         torch = self.torch
         torch.cuda.synchronize()
-        e = self._as_u32(self._counter + 128)
-        self.epoch = int(e.item())
-
-    def _as_u32(self, ptr):
-        torch = self.torch
-
-        class _Arr:
-            __cuda_array_interface__ = {"shape": (1,), "typestr": "<u4", "data": (ptr, False), "version": 3,
-                                        "strides": None}
-        return torch.as_tensor(_Arr(), device="cuda").to(torch.int64)
+        self.epoch = int(_u32_view(torch, self._counter + 128).item())
 
     def close(self):
         torch = self.torch
@@ -171,3 +162,120 @@ class FusedColumnParallel:
         for p in self._own:
             L.lbc_device_free(p)
         self._own = []
+
+
+class FusedColumnParallelGemm:
+    """Many-token GEMM (64+ tokens, any of the three formats) with the
+    all-gather fused into the tcgen05 prefill kernel's store
+    (``lbc_gemm_allgather``): every finished output tile goes to every rank's
+    Y over NVLink while later tiles are computed, so the exchange overlaps the
+    GEMM instead of following it. Y is double-buffered by call parity (a rank
+    can start call e + 1 while a peer still reads Y(e); call e + 2 waits for
+    every rank's call e + 1, which follows that rank's reads of Y(e) in its
+    stream); each rank's device call counter (CUDA-graph replays stay correct)
+    and one call counter per rank pair signal completion. ``__call__`` returns
+    the Y of the call it launched (by the host's count of calls)."""
+
+    KINDS = {"w4a16": 0, "mxfp4": 1, "w4a8": 2}
+
+    def __init__(self, kind: str, m: int, n: int, group=None):
+        import ctypes as C
+        import torch
+        import torch.distributed as dist
+        from . import kernels as K
+        if kind not in self.KINDS:
+            raise ValueError(f"kind must be one of {sorted(self.KINDS)}")
+        if m < 64:
+            raise ValueError("the fused all-gather GEMM serves 64 or more tokens")
+        self.K, self.C, self.torch = K, C, torch
+        self.kind, self.group = kind, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.m, self.n = m, n
+        self.lo, self.hi = shard_bounds(n, self.rank, self.world)
+        L = K.lib()
+        self._own = []
+
+        def alloc(nbytes):
+            p = C.c_void_p()
+            K._check(L.lbc_device_alloc(nbytes, C.byref(p)), "lbc_device_alloc")
+            self._own.append(p.value)
+            return p.value
+
+        half = m * n * 4
+        self._y = alloc(2 * half)
+        self._flags = alloc(max(16, 4 * self.world))
+        self._counter = alloc(256)  # byte 0: CTA counter, byte 128: call epoch
+        handles = []
+        for ptr in (self._y, self._flags):
+            h = (C.c_char * 64)()
+            K._check(L.lbc_ipc_get_handle(ptr, h), "lbc_ipc_get_handle")
+            handles.append(bytes(h))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, handles, group=group)
+        self._opened = []
+        ys, fs = [], []
+        for r, (hy, hf) in enumerate(everyone):
+            if r == self.rank:
+                ys.append(self._y)
+                fs.append(self._flags)
+                continue
+            for h, out in ((hy, ys), (hf, fs)):
+                p = C.c_void_p()
+                buf = (C.c_char * 64).from_buffer_copy(h)
+                K._check(L.lbc_ipc_open_handle(buf, C.byref(p)), "lbc_ipc_open_handle")
+                self._opened.append(p.value)
+                out.append(p.value)
+        dev = torch.cuda.current_device()
+        self._yptrs = torch.tensor([y + par * half for par in (0, 1) for y in ys], dtype=torch.int64, device=dev)
+        self._fptrs = torch.tensor(fs, dtype=torch.int64, device=dev)
+        self._yview = [_f32_view(torch, self._y + par * half, (m, n)) for par in (0, 1)]
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def __call__(self, x, w_local, params=None, _prep=None):
+        K, C = self.K, self.C
+        self.epoch += 1
+        pr = _prep or K._Prepared(x, w_local.kp, w_local.n)
+        d = K._dev_weights(w_local)
+        ptr = (lambda t: None if t is None else t.data_ptr())
+        rc = K.lib().lbc_gemm_allgather(
+            self.KINDS[self.kind], pr.x.data_ptr(), pr.m, w_local.kp, d.qw.data_ptr(),
+            ptr(getattr(d, "scales", None)), ptr(getattr(d, "zeros", None)), ptr(getattr(d, "e8m0", None)),
+            w_local.n, self.lo, self.n, self._yptrs.data_ptr(), self._fptrs.data_ptr(), self._counter,
+            self._counter + 128, self.rank, self.world, C.byref(K._params(params, None)), K._stream())
+        K._check(rc, "lbc_gemm_allgather")
+        return self._yview[self.epoch & 1]
+
+    def resync(self):
+        """Re-read the device call counter (after CUDA-graph replays of these calls)."""
+        torch = self.torch
+        torch.cuda.synchronize()
+        self.epoch = int(_u32_view(torch, self._counter + 128).item())
+
+    def close(self):
+        torch = self.torch
+        torch.cuda.synchronize()
+        L = self.K.lib()
+        for p in self._opened:
+            L.lbc_ipc_close_handle(p)
+        self._opened = []
+        torch.distributed.barrier(group=self.group)
+        for p in self._own:
+            L.lbc_device_free(p)
+        self._own = []
+
+
+def _f32_view(torch, ptr, shape):
+    """A float32 CUDA tensor aliasing library-owned device memory."""
+    class _Arr:
+        __cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+    return torch.as_tensor(_Arr(), device="cuda")
+
+
+def _u32_view(torch, ptr):
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (1,), "typestr": "<u4", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+    return torch.as_tensor(_Arr(), device="cuda").to(torch.int64)

@@ -269,3 +269,30 @@ def test_key_split_attention(B, S, pos):
             s = (kd[b, h // G] @ qd[b, h]) / np.sqrt(D)
             ref[b, h] = torch.softmax(s, 0) @ vd[b, h // G]
     assert float((o1.double().cpu().view(B, H, D) - ref).abs().max()) < 1e-4
+
+
+@pytest.mark.parametrize("backend", ["w4a16", "w4a8"])
+def test_profile_sections(backend):
+    """Model.prof (the reference's Profile, src/lowbit/model.py:243-261): with
+    profiling on, prefill and graph-replayed decode record device time in the
+    reference's four sections; results are identical with it off; the
+    sections of a decode step sum to no more than the step's wall time."""
+    key = next(k for k in KEYS if k.endswith("_" + backend))
+    m, toks, _ = build(key)
+    c = m.new_cache(len(toks) + 12)
+    ref = m.generate(toks, 10, cache=c)
+    m.prof.enabled = True
+    m.prof.reset()
+    c.reset()
+    t = {}
+    got = m.generate(toks, 10, cache=c, timings=t)
+    assert got == ref
+    prof = dict(m.prof.t)
+    assert set(prof) == {"linear", "attention", "lm_head", "other"}, prof
+    assert all(v > 0 for v in prof.values()), prof
+    assert sum(prof.values()) <= t["prefill_s"] + t["decode_s"], (prof, t)
+    m.prof.enabled = False
+    m.prof.reset()
+    c.reset()
+    assert m.generate(toks, 10, cache=c) == ref
+    assert dict(m.prof.t) == {}
