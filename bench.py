@@ -859,6 +859,7 @@ def run_model(args) -> dict:
         g.replay()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
+    del g  # a graph holding NCCL calls must be gone before the process group
 
     # per-section device time (Model.prof, the reference's linear / attention /
     # lm_head / other split) of one profiled generation, untimed: the prompt's
@@ -896,8 +897,9 @@ def run_model(args) -> dict:
             "config": {"workload": "Qwen2-0.5B-shaped decoder, w4a16 asym linears, prompt 128, 128 greedy tokens "
                                    "(BASELINE configs[4])", "layers": cfg.num_layers, "hidden": cfg.hidden_size,
                        "vocab": V, "prompt": P, "new_tokens": NEW,
-                       "parallelism": (f"tensor parallel x{world}: column-parallel linears + NCCL all-gather, "
-                                       "norms / RoPE / attention replicated" if world > 1 else "one GPU"),
+                       "parallelism": (f"tensor parallel x{world}: column-parallel linears (decode GEMVs with the "
+                                       "all-gather fused in, NCCL all-gather otherwise), norms / RoPE / attention "
+                                       "replicated" if world > 1 else "one GPU"),
                        "timing": "decode: 127 CUDA-graph replays of a whole decode step (host clock around "
                                  "synchronised loops, max over ranks); a step = one token for every sequence "
                                  "of the batch"},
@@ -945,7 +947,9 @@ def run_model(args) -> dict:
                "the one-GPU run reports it" if world > 1 else "unavailable: oracle/_ref/liblowbit_ref.so not built")
         line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": 0, "kind": "reference", "sample": why}
     if world > 1:
+        import gc
         m.release_graphs()  # they hold NCCL calls
+        gc.collect()
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
