@@ -79,6 +79,9 @@ struct GemvArgs {
 constexpr int XM_PLAIN = 0;    // x as given
 constexpr int XM_RMSNORM = 1;  // (x + xres) / sqrt(mean((x + xres)^2) + eps) * lnw
 constexpr int XM_GLU = 2;      // silu(x[:, :Kp]) * x[:, Kp:] (x rows of 2 * Kp)
+constexpr int XM_QUANT = 3;    // W4A8 from fp32 x: the per-token int8 quantizer inside the kernel
+constexpr int QUANT_CLUSTER = 8;   // CTAs per cluster sharing one quantization (XM_QUANT)
+constexpr int QUANT_MAX_KP = 8192; // XM_QUANT rows (the slices of one cluster fit in shared memory)
 
 // Per-stage metadata region (scales + zero points, or E8M0 exponents) when it
 // is staged by TMA: bytes per row of each part, rounded regions per stage.

@@ -29,12 +29,15 @@
 // previous kernel in the stream).
 //
 // Work split: CTA c owns the rows [c*N/P, (c+1)*N/P) (P = grid size), i.e.
-// the same number of weight bytes +-1 row; its rows form blocks of 16 (the
-// last one possibly partial), and the (block, group) units are split into
-// contiguous ranges over the CTA's warps. Each warp streams its units' codes
-// straight from HBM into registers (16-byte loads, L1 no-allocate, L2
-// evict-first), DEPTH units ahead of the decode; its per-block partial sums go
-// to shared memory slots, which the CTA adds in warp order (deterministic).
+// the same number of weight bytes +-1 row, in blocks of 16 rows (the last
+// one possibly partial). A producer warp copies each stage -- one row block
+// x one K segment -- into a shared-memory ring with one 1-D bulk copy per
+// row (the TMA engine, no multicast), completion counted on the stage's
+// mbarrier; the consumer warps split each stage's groups, copy their words
+// to registers and release the slot before decoding. The CTA's scales and
+// zero points are loaded into shared memory once, before griddepcontrol.wait.
+// Each warp's per-block partial sums go to shared memory slots, which the CTA
+// adds in warp order (deterministic).
 #pragma once
 
 #include <cuda_bf16.h>
