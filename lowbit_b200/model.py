@@ -361,7 +361,8 @@ class ColumnParallelLinear(Linear):
         self.b = None if b is None else to_cuda(np.asarray(b, np.float32))
         self.threads = inner.threads
         self.nbytes = inner.nbytes
-        self.lo, self.hi = shard_bounds(n, dist.get_rank(group), dist.get_world_size(group))
+        self._world = dist.get_world_size(group)
+        self.lo, self.hi = shard_bounds(n, dist.get_rank(group), self._world)
         self._cps: dict = {}
         self._fused = fused_pool
 
@@ -381,7 +382,7 @@ class ColumnParallelLinear(Linear):
         from .sharding import ColumnParallel, FusedColumnParallel
         m = int(x.shape[0])
         if (self._fused is not None and m <= 2 and self.kind == "w4a16" and self.params is None
-                and self.inner.wq.kp % 128 == 0):
+                and self.inner.wq.kp % 128 == 0 and self._world <= 8):
             fc = self._fused.get((m, self.n))
             if fc is None:
                 fc = self._fused[(m, self.n)] = FusedColumnParallel(m, self.n, self.group)

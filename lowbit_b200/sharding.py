@@ -66,6 +66,61 @@ def gemm_sharded(kind: str, x, w_local, cp: ColumnParallel, **kw):
     return cp.gather(y)
 
 
+class _PeerBuffers:
+    """Library-owned device buffers of this rank, mapped by every rank of the
+    process group over CUDA IPC (`lbc_device_alloc`, zero-filled), plus
+    private ones that stay local. `peers(name)` lists a shared buffer's
+    address on every rank, in rank order (this rank's own included).
+    `close()` is collective: every rank unmaps the peers' buffers, then
+    frees its own once nobody maps them."""
+
+    def __init__(self, group, shared: dict, private: dict):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import kernels as K
+        self.K, self.C, self.dist, self.group = K, C, dist, group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        L = K.lib()
+        self._own, self._opened, self.addr, self._peers = [], [], {}, {}
+        for name, nbytes in list(shared.items()) + list(private.items()):
+            p = C.c_void_p()
+            K._check(L.lbc_device_alloc(nbytes, C.byref(p)), "lbc_device_alloc")
+            self._own.append(p.value)
+            self.addr[name] = p.value
+        handles = []
+        for name in shared:
+            h = (C.c_char * 64)()
+            K._check(L.lbc_ipc_get_handle(self.addr[name], h), "lbc_ipc_get_handle")
+            handles.append(bytes(h))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, handles, group=group)
+        for i, name in enumerate(shared):
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self.addr[name])
+                    continue
+                p = C.c_void_p()
+                buf = (C.c_char * 64).from_buffer_copy(everyone[r][i])
+                K._check(L.lbc_ipc_open_handle(buf, C.byref(p)), "lbc_ipc_open_handle")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            self._peers[name] = ptrs
+
+    def peers(self, name: str) -> list:
+        return self._peers[name]
+
+    def close(self):
+        L = self.K.lib()
+        for p in self._opened:
+            L.lbc_ipc_close_handle(p)
+        self._opened = []
+        self.dist.barrier(group=self.group)  # no rank maps this rank's buffers any more
+        for p in self._own:
+            L.lbc_device_free(p)
+        self._own = []
+
+
 class FusedColumnParallel:
     """W4A16 decode (one or two tokens) with the all-gather fused into the
     kernel (``lbc_gemm_w4a16_allgather``): every rank's GEMV writes its own Y
@@ -98,32 +153,11 @@ class FusedColumnParallel:
             raise ValueError("the fused all-gather decode serves at most 8 ranks")
         self.m, self.n = m, n
         self.lo, self.hi = shard_bounds(n, self.rank, self.world)
-        L = K.lib()
-        self._own = []
-
-        def alloc(nbytes):
-            p = C.c_void_p()
-            K._check(L.lbc_device_alloc(nbytes, C.byref(p)), "lbc_device_alloc")
-            self._own.append(p.value)
-            return p.value
-
-        self._land = alloc(n * 2 * 2 * 8)   # LBC_GATHER_LAND_BYTES(n)
-        self._counter = alloc(256)          # byte 0: CTA counter, byte 128: call epoch
-        h = (C.c_char * 64)()
-        K._check(L.lbc_ipc_get_handle(self._land, h), "lbc_ipc_get_handle")
-        everyone = [None] * self.world
-        dist.all_gather_object(everyone, bytes(h), group=group)
-        self._opened = []
-        lands = []
-        for r, hr in enumerate(everyone):
-            if r == self.rank:
-                lands.append(self._land)
-                continue
-            p = C.c_void_p()
-            buf = (C.c_char * 64).from_buffer_copy(hr)
-            K._check(L.lbc_ipc_open_handle(buf, C.byref(p)), "lbc_ipc_open_handle")
-            self._opened.append(p.value)
-            lands.append(p.value)
+        # landing buffer: LBC_GATHER_LAND_BYTES(n); counters: byte 0 the CTA
+        # counter, byte 128 the call epoch
+        self._buf = _PeerBuffers(group, {"land": n * 2 * 2 * 8}, {"counter": 256})
+        self._counter = self._buf.addr["counter"]
+        lands = self._buf.peers("land")
         dev = torch.cuda.current_device()
         self._lptrs = torch.tensor(lands, dtype=torch.int64, device=dev)
         self._ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(2)]
@@ -151,17 +185,8 @@ class FusedColumnParallel:
         self.epoch = int(_u32_view(torch, self._counter + 128).item())
 
     def close(self):
-        torch = self.torch
-        torch.cuda.synchronize()
-        L = self.K.lib()
-        for p in self._opened:
-            L.lbc_ipc_close_handle(p)
-        self._opened = []
-        # no peer maps this rank's landing buffer any more once all have closed
-        self.torch.distributed.barrier(group=self.group)
-        for p in self._own:
-            L.lbc_device_free(p)
-        self._own = []
+        self.torch.cuda.synchronize()
+        self._buf.close()
 
 
 class FusedColumnParallelGemm:
@@ -193,39 +218,12 @@ class FusedColumnParallelGemm:
         self.rank = dist.get_rank(group)
         self.m, self.n = m, n
         self.lo, self.hi = shard_bounds(n, self.rank, self.world)
-        L = K.lib()
-        self._own = []
-
-        def alloc(nbytes):
-            p = C.c_void_p()
-            K._check(L.lbc_device_alloc(nbytes, C.byref(p)), "lbc_device_alloc")
-            self._own.append(p.value)
-            return p.value
-
         half = m * n * 4
-        self._y = alloc(2 * half)
-        self._flags = alloc(max(16, 4 * self.world))
-        self._counter = alloc(256)  # byte 0: CTA counter, byte 128: call epoch
-        handles = []
-        for ptr in (self._y, self._flags):
-            h = (C.c_char * 64)()
-            K._check(L.lbc_ipc_get_handle(ptr, h), "lbc_ipc_get_handle")
-            handles.append(bytes(h))
-        everyone = [None] * self.world
-        dist.all_gather_object(everyone, handles, group=group)
-        self._opened = []
-        ys, fs = [], []
-        for r, (hy, hf) in enumerate(everyone):
-            if r == self.rank:
-                ys.append(self._y)
-                fs.append(self._flags)
-                continue
-            for h, out in ((hy, ys), (hf, fs)):
-                p = C.c_void_p()
-                buf = (C.c_char * 64).from_buffer_copy(h)
-                K._check(L.lbc_ipc_open_handle(buf, C.byref(p)), "lbc_ipc_open_handle")
-                self._opened.append(p.value)
-                out.append(p.value)
+        # Y of both parities, the call counters [world] of the rank pairs, and
+        # this rank's CTA counter (byte 0) and call epoch (byte 128)
+        self._buf = _PeerBuffers(group, {"y": 2 * half, "flags": max(16, 4 * self.world)}, {"counter": 256})
+        self._y, self._counter = self._buf.addr["y"], self._buf.addr["counter"]
+        ys, fs = self._buf.peers("y"), self._buf.peers("flags")
         dev = torch.cuda.current_device()
         self._yptrs = torch.tensor([y + par * half for par in (0, 1) for y in ys], dtype=torch.int64, device=dev)
         self._fptrs = torch.tensor(fs, dtype=torch.int64, device=dev)
@@ -254,16 +252,8 @@ class FusedColumnParallelGemm:
         self.epoch = int(_u32_view(torch, self._counter + 128).item())
 
     def close(self):
-        torch = self.torch
-        torch.cuda.synchronize()
-        L = self.K.lib()
-        for p in self._opened:
-            L.lbc_ipc_close_handle(p)
-        self._opened = []
-        torch.distributed.barrier(group=self.group)
-        for p in self._own:
-            L.lbc_device_free(p)
-        self._own = []
+        self.torch.cuda.synchronize()
+        self._buf.close()
 
 
 def _f32_view(torch, ptr, shape):
