@@ -409,6 +409,51 @@ bool want_mma(const lbc_params *p, int fmt, int M, int N, int Kp) {
   return p && p->isa == LBC_PATH_MMA;
 }
 
+// W4A8 on mma.sync.m16n8k32 s8 (gemv_i8mma.cu): 8 or 16 tokens per pass
+// (n-blocks of 8), nr = warps per CTA (4 or 8; default 8), nb = CTAs per SM
+// (default: up to 4, as many as fit)
+struct I8Plan {
+  int nb = 1, nw = 8, passes = 1, grid = 1, smem = 0, cps = 1;
+};
+
+int plan_i8mma(int M, int N, int Kp, const lbc_params *p, I8Plan &P) {
+  const DevInfo di = dev_info();
+  if (M > 16) return fail(LBC_ERR_PARAMS, "w4a8 mma path: at most 16 tokens");
+  P.nb = M <= 8 ? 1 : 2;
+  P.passes = ceil_div(M, 8 * P.nb);
+  P.nw = (p && p->nr > 0) ? p->nr : 8;
+  if (P.nw != 4 && P.nw != 8) return fail(LBC_ERR_PARAMS, "w4a8 mma path: 4 or 8 warps per CTA (nr)");
+  P.smem = lbc::i8mma_smem(P.nb, P.nw, Kp);
+  if (P.smem > di.smem_optin) return fail(LBC_ERR_PARAMS, "w4a8 mma path: the activations do not fit in shared memory");
+  const int occ = lbc::i8mma_occupancy(P.nb, P.nw, P.smem);
+  if (occ <= 0) return fail(LBC_ERR_PARAMS, "w4a8 mma path: kernel cannot be resident on an SM");
+  P.cps = std::min((p && p->nb > 0) ? p->nb : 4, occ);
+  P.grid = std::max(1, std::min(ceil_div(N, 16), di.sms * P.cps));
+  return 0;
+}
+
+// The int8 MMA kernel serves W4A8 on request (isa = LBC_PATH_MMA) and,
+// automatically with default tiling, 8-16 tokens, and 3-7 tokens whose rows
+// are too long for the decode kernel (measured on the BASELINE shapes: 1.2-2x
+// over the decode / staged / tcgen05 kernels there; the decode kernel stays
+// faster at 1-4 tokens on rows it takes)
+bool want_i8mma(const lbc_params *p, int M, int N, int Kp) {
+  (void)N;
+  if (p && p->isa == LBC_PATH_MMA) return true;
+  if (!path_auto(p) || (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0))) return false;
+  if (M < 3 || M > 16 || lbc::i8mma_smem(M <= 8 ? 1 : 2, 8, Kp) > dev_info().smem_optin) return false;
+  return M >= 8 || !rows_eligible(lbc::FMT_W4A8, M, Kp, p);
+}
+
+int run_i8mma(lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
+  I8Plan P;
+  if (int rc = plan_i8mma(a.M, a.N, a.Kp, p, P)) return rc;
+  a.status = dev_info().status;
+  cudaError_t e = lbc::i8mma_launch(a, P.nb, P.nw, dim3(P.grid, P.passes, 1), st);
+  if (e != cudaSuccess) return fail_cuda("w4a8 mma gemm launch", e);
+  return LBC_PATH_MMA;
+}
+
 int run_mma(int fmt, lbc::GemvArgs a, const lbc_params *p, cudaStream_t st) {
   MmaPlan P;
   if (int rc = plan_mma(fmt, a.M, a.N, a.Kp, p, P)) return rc;
@@ -606,6 +651,15 @@ int lbc_describe_plan(int kind, int M, int N, int Kp, const lbc_params *p, char 
   if (int rc = check_shape(M, Kp, N, kind == 1 ? LBC_MXBLOCK : LBC_GROUP)) return rc;
   if (int rc = device_gate()) return rc;
   const int fmt = kind == 0 ? lbc::FMT_W4A16 : kind == 1 ? lbc::FMT_MXFP4 : lbc::FMT_W4A8;
+  if (fmt == lbc::FMT_W4A8 && want_i8mma(p, M, N, Kp)) {
+    I8Plan P;
+    if (int rc = plan_i8mma(M, N, Kp, p, P)) return rc;
+    if (buf && buflen > 0)
+      snprintf(buf, (size_t)buflen,
+               "{\"path\": \"mma\", \"kernel\": \"i8mma\", \"nblocks\": %d, \"warps\": %d, \"passes\": %d, "
+               "\"grid\": %d, \"ctas_per_sm\": %d, \"smem\": %d}", P.nb, P.nw, P.passes, P.grid, P.cps, P.smem);
+    return LBC_PATH_MMA;
+  }
   if (want_mma(p, fmt, M, N, Kp)) {
     MmaPlan P;
     if (int rc = plan_mma(fmt, M, N, Kp, p, P)) return rc;
@@ -726,7 +780,7 @@ int lbc_gemm_w4a16_glu(const float *gu, int M, int Kp, const uint8_t *qw, const 
 int lbc_gemm_mxfp4(const float *x, int M, int Kp, const uint8_t *qw, const uint8_t *e8m0, int N,
                    float *y, const lbc_params *p, void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_MXBLOCK)) return rc;
-  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 only");
+  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma path: W4A16 and W4A8 only");
   if (!x || !qw || !e8m0 || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
@@ -764,10 +818,15 @@ int lbc_gemm_w4a8_q(const int8_t *xq, const float *xs, const int32_t *asum, int 
                     const uint8_t *qw, const float *scales, const uint8_t *zeros, int N, float *y,
                     const lbc_params *p, void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
-  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 only");
   if (!xq || !xs || !asum || !qw || !scales || !y || !al16(xq) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (xq, qw need 16-byte alignment)");
   if (int rc = device_gate()) return rc;
+  if (want_i8mma(p, M, N, Kp)) {
+    lbc::GemvArgs a{};
+    a.xq = xq; a.xs = xs; a.asum = asum; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+    a.M = M; a.N = N; a.Kp = Kp;
+    return run_i8mma(a, p, static_cast<cudaStream_t>(stream));
+  }
   if (want_tc(p, lbc::FMT_W4A8, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
@@ -790,7 +849,7 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
                   const uint8_t *zeros, int N, float *y, const lbc_params *p, void *workspace,
                   void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
-  if (p && p->isa == LBC_PATH_MMA) return fail(LBC_ERR_PARAMS, "mma decode path: W4A16 only");
+  if (p && p->isa == LBC_PATH_MMA && M > 16) return fail(LBC_ERR_PARAMS, "w4a8 mma path: at most 16 tokens");
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))
@@ -816,7 +875,12 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
   int rc = 0;
   cudaError_t e = lbc::launch_quant_act_int8(x, M, Kp, xq, xs, asum, st);
   if (e != cudaSuccess) rc = fail_cuda("quant_act_int8 launch", e);
-  if (rc == 0 && want_tc(p, lbc::FMT_W4A8, M, N, Kp)) {
+  if (rc == 0 && want_i8mma(p, M, N, Kp)) {
+    lbc::GemvArgs a{};
+    a.xq = xq; a.xs = xs; a.asum = asum; a.qw = qw; a.scales = scales; a.zeros = zeros; a.y = y;
+    a.M = M; a.N = N; a.Kp = Kp;
+    rc = run_i8mma(a, p, st);
+  } else if (rc == 0 && want_tc(p, lbc::FMT_W4A8, M, N, Kp)) {
     lbc::TcCall c{};
     c.fmt = lbc::FMT_W4A8; c.xq = xq; c.xs = xs; c.asum = asum; c.qw = qw; c.scales = scales;
     c.zeros = zeros; c.y = y; c.M = M; c.N = N; c.Kp = Kp;

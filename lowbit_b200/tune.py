@@ -5,13 +5,15 @@ save_cache, the same two-stage search and cache-entry fields).
 Stage 1 picks the kernel path and the shape of the work: the automatic
 choice, then every alternative the planner accepts for the problem (for one
 or two tokens the register-streamed decode kernel at 2-8 CTAs per SM and the
-warp-level tensor-core kernel at several tilings; for 3-63 tokens the
+warp-level tensor-core kernel at several tilings (W4A16); for W4A8 with up
+to 16 tokens the int8 mma.sync kernel at 4 and 8 warps; for 3-63 tokens the
 tcgen05 exact kernel; from 64 tokens the exact kernel beside the bf16
 prefill kernel; below 64 tokens the staged SIMT kernel at every compiled
 tokens-per-pass x rows-per-team). Stage 2 refines the three fastest: pipeline
 stages (`order`), CTAs per SM (`nb`) and split-K length (`kb`) for the
 staged kernel, CTAs per SM for the decode kernel, warps / K per stage / ring
-depth for the tensor-core decode kernel.
+depth for the tensor-core decode kernel, warps and CTAs per SM for the int8
+mma kernel.
 
 Every candidate is timed as the library is used: a CUDA graph of `steps`
 calls over a pool of weight copies larger than twice the L2 cache (each call
@@ -88,7 +90,9 @@ def _stage1(kind: str, m: int) -> list[K.Params]:
         if kind == "w4a16":                                      # warp-level tensor-core kernel
             c += [P(isa="mma", nr=nw, kb=kb, order=ns) for nw, kb, ns in
                   ((8, 4096, 2), (8, 2048, 4), (16, 4096, 3), (4, 2048, 4), (16, 2048, 4))]
-    else:
+    if kind == "w4a8" and m <= 16:                               # int8 mma.sync kernel
+        c += [P(isa="mma", nr=8), P(isa="mma", nr=4)]
+    if m > 2:
         c.append(P(isa="tcgen05", mr=16))                        # tcgen05 exact kernel
     if m < 64:
         for mt in (1, 2, 4, 8):                                  # staged SIMT kernel
@@ -102,7 +106,9 @@ def _stage1(kind: str, m: int) -> list[K.Params]:
 def _stage2(kind: str, m: int, kp: int, base: K.Params) -> list[K.Params]:
     P = K.Params
     out = []
-    if base.isa == "mma":
+    if base.isa == "mma" and kind == "w4a8":
+        out += [P(isa="mma", nr=nw, nb=nb) for nw in (4, 8) for nb in (1, 2, 3, 4)]
+    elif base.isa == "mma":
         for nw, kb in ((8, 4096), (8, 2048), (16, 4096), (16, 2048), (4, 2048)):
             for ns in (2, 3, 4):
                 for nb in (1, 2):

@@ -102,18 +102,23 @@ def test_decode_nan_scale_propagates(rng):
 @pytest.mark.parametrize("n", [1, 333])
 @pytest.mark.parametrize("asym", [False, True])
 def test_decode_w4a8_several_tokens(rng, m, k, n, asym):
-    """W4A8 with 3-16 tokens runs the decode kernel 4 or 8 tokens per pass
-    (rows of up to 8192 elements); results meet the W4A8 bound, exact int32
-    group sums included."""
+    """W4A8 with 3-16 tokens: the automatic path (the decode kernel 4 or 8
+    tokens per pass below 8 tokens, the int8 mma kernel from 8) and the
+    decode kernel forced by isa="simt" (rows of up to 8192 elements) meet the
+    W4A8 bound, exact int32 group sums included."""
     x, w = _problem(rng, m, n, k)
     W = lb.quantize_int4(w, asym=asym)
     plan = K.describe_plan("w4a8", m, n, W.kp)
+    assert plan["kernel"] == ("i8mma" if m >= 8 else "rows"), plan
+    simt = K.Params(isa="simt")
+    plan = K.describe_plan("w4a8", m, n, W.kp, simt)
     assert plan["kernel"] == "rows" and plan["mt"] == (4 if m <= 4 else 8), plan
     a = lb.quantize_act_int8(x)
     ref = R.gemm_w4a8_ref(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
     bound = R.w4a8_bound(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
-    R.assert_close(K.gemm_w4a8(x, W), ref, bound, RTOL)
-    R.assert_close(K.gemm_w4a8_q(a, W), ref, bound, RTOL)
+    for p in (None, simt):
+        R.assert_close(K.gemm_w4a8(x, W, p), ref, bound, RTOL)
+        R.assert_close(K.gemm_w4a8_q(a, W, p), ref, bound, RTOL)
 
 
 @pytest.mark.parametrize("m", [5, 8, 16])
