@@ -16,10 +16,11 @@
 // 16t + 4i + [0, 4) (low nibbles) and 64 + 16t + 4i + [0, 4) (high): the A
 // registers of k-step i for logical k = 4t + [0, 4) and 16 + 4t + [0, 4).
 // The B fragment of token column c at k-step i is then the two 32-bit words
-// of xq at those element positions, staged once per CTA in shared memory in
-// fragment order (conflict-free 8-byte reads). Decoding a word into two s8
-// quads: (w & 0x0F0F0F0F) | 0x80808080 is 128 + q per byte, minus z per byte
-// (no borrow: 128 + q - z >= 113), then xor 0x80 gives q - z.
+// of xq at those element positions, staged by each warp for its own groups
+// in shared memory in fragment order (conflict-free 8-byte reads). Decoding
+// a word into two s8 quads: (w & 0x0F0F0F0F) | 0x80808080 is 128 + q per
+// byte, minus z per byte (no borrow: 128 + q - z >= 113), then xor 0x80
+// gives q - z.
 //
 // Work: CTA c owns the 16-row blocks [c*B/P, (c+1)*B/P); its warps split
 // every block's groups; each warp streams its (block, group) units' codes
@@ -54,13 +55,13 @@ constexpr int I8_DEPTH = 4;  // units of codes in flight per warp ahead of the M
 }  // namespace
 
 // Dynamic shared memory: B fragments [G][4 k-steps][NB][32 lanes] uint2, the
-// warps' partial sums [NW][16 rows][8 NB tokens] fp32, token scales [8 NB].
+// warps' partial sums [NW][8 NB tokens][16 rows] fp32, token scales [8 NB].
 __host__ __device__ inline int i8mma_smem_bytes(int nb, int nw, int Kp) {
   return (Kp / 128) * 4 * nb * 32 * 8 + nw * 16 * 8 * nb * 4 + 8 * nb * 4;
 }
 
 template <int NB, int NW>
-__global__ void __launch_bounds__(NW * 32) w4a8_mma_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(NW * 32, 2) w4a8_mma_kernel(const GemvArgs a) {
   constexpr int TOK = 8 * NB;
   extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -112,45 +113,45 @@ __global__ void __launch_bounds__(NW * 32) w4a8_mma_kernel(const GemvArgs a) {
   pdl_launch_dependents();
   pdl_wait_prior_grid();
 
-  // B fragments of this pass's tokens for every group, in fragment order.
-  // Item (g, n-block, lane) = the two 16-byte runs of its token's codes at
-  // 16t and 64 + 16t in group g: word j of each is the fragment of k-step j.
-  // Four items' loads are issued before their stores (plain loads: the
-  // griddepcontrol.wait above orders them after the producer kernel).
-  {
-    const int items = G * NB * 32;
-    for (int base = tid; base < items; base += NW * 32 * 4) {
-      uint4 lo[4], hi[4];
+  // B fragments of this pass's tokens for this warp's groups, in fragment
+  // order (each warp reads only its own groups', so only a warp-level sync
+  // stands between its staging and its MMAs). Item (g, n-block, lane) = the
+  // two 16-byte runs of its token's codes at 16t and 64 + 16t in group g:
+  // word j of each is the fragment of k-step j. All of a lane's loads are
+  // issued before their stores (plain loads: the griddepcontrol.wait above
+  // orders them after the producer kernel).
+  static_assert(NB <= 2, "at most two n-blocks");
+  constexpr int QMAX = 4 / NB;  // groups per warp staged per round
+  for (int q0 = 0; q0 < ng; q0 += QMAX) {
+    uint4 lo[QMAX][NB], hi[QMAX][NB];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int it = base + r * NW * 32;
-        lo[r] = hi[r] = make_uint4(0u, 0u, 0u, 0u);
-        if (it < items) {
-          const int ln = it & 31, nb = (it >> 5) % NB, g = (it >> 5) / NB;
-          const int m = m0 + nb * 8 + (ln >> 2);
-          if (m < a.M) {
-            const int8_t *row = a.xq + (size_t)m * a.Kp + (g << 7) + (ln & 3) * 16;
-            lo[r] = *reinterpret_cast<const uint4 *>(row);
-            hi[r] = *reinterpret_cast<const uint4 *>(row + 64);
-          }
+    for (int q = 0; q < QMAX; ++q)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        lo[q][nb] = hi[q][nb] = make_uint4(0u, 0u, 0u, 0u);
+        const int m = m0 + nb * 8 + gq;
+        if (q0 + q < ng && m < a.M) {
+          const int8_t *row = a.xq + (size_t)m * a.Kp + ((wg0 + q0 + q) << 7) + tq * 16;
+          lo[q][nb] = *reinterpret_cast<const uint4 *>(row);
+          hi[q][nb] = *reinterpret_cast<const uint4 *>(row + 64);
         }
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int it = base + r * NW * 32;
-        if (it < items) {
-          const int ln = it & 31, nb = (it >> 5) % NB, g = (it >> 5) / NB;
-          uint2 *dst = bfrag + ((size_t)g * 4 * NB + nb) * 32 + ln;
-          dst[0] = make_uint2(lo[r].x, hi[r].x);
-          dst[NB * 32] = make_uint2(lo[r].y, hi[r].y);
-          dst[2 * NB * 32] = make_uint2(lo[r].z, hi[r].z);
-          dst[3 * NB * 32] = make_uint2(lo[r].w, hi[r].w);
+    for (int q = 0; q < QMAX; ++q)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        if (q0 + q < ng) {
+          uint2 *dst = bfrag + ((size_t)(wg0 + q0 + q) * 4 * NB + nb) * 32 + lane;
+          dst[0] = make_uint2(lo[q][nb].x, hi[q][nb].x);
+          dst[NB * 32] = make_uint2(lo[q][nb].y, hi[q][nb].y);
+          dst[2 * NB * 32] = make_uint2(lo[q][nb].z, hi[q][nb].z);
+          dst[3 * NB * 32] = make_uint2(lo[q][nb].w, hi[q][nb].w);
         }
       }
-    }
   }
-  for (int e = tid; e < TOK; e += NW * 32) xs_s[e] = (m0 + e < a.M) ? ld_act(a.xs + m0 + e) : 0.f;
-  __syncthreads();
+  for (int e = lane; e < TOK; e += 32)
+    if (warp == 0) xs_s[e] = (m0 + e < a.M) ? ld_act(a.xs + m0 + e) : 0.f;
+  __syncwarp();
 
   float y[NB][4];
   int u = 0;
@@ -201,25 +202,26 @@ __global__ void __launch_bounds__(NW * 32) w4a8_mma_kernel(const GemvArgs a) {
         default: unit(std::integral_constant<int, 3>{}); break;
       }
     }
-    // the block's partial sums: [warp][row][token]; D fragment (row gq, token
-    // 2tq + e) and (row gq + 8, token 2tq + e) of each n-block
+    // the block's partial sums, token-major: [warp][token][row]; D fragment
+    // (row gq, token 2tq + e) and (row gq + 8, token 2tq + e) of each n-block
     float *pw = part + warp * 16 * TOK;
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const int c = nb * 8 + 2 * tq;
-      pw[gq * TOK + c] = y[nb][0];
-      pw[gq * TOK + c + 1] = y[nb][1];
-      pw[(gq + 8) * TOK + c] = y[nb][2];
-      pw[(gq + 8) * TOK + c + 1] = y[nb][3];
+      pw[c * 16 + gq] = y[nb][0];
+      pw[(c + 1) * 16 + gq] = y[nb][1];
+      pw[c * 16 + gq + 8] = y[nb][2];
+      pw[(c + 1) * 16 + gq + 8] = y[nb][3];
     }
     __syncthreads();
     // sums over the warps in warp order (deterministic), token scale, store:
-    // consecutive threads hold consecutive rows of one token
+    // consecutive threads hold consecutive rows of one token (conflict-free
+    // reads, 64-byte runs of Y)
     for (int e = tid; e < 16 * TOK; e += NW * 32) {
       const int r = e & 15, c = e >> 4;
       const int n = rb * 16 + r, m = m0 + c;
       float v = 0.f;
-      for (int ww = 0; ww < NW; ++ww) v += part[(ww * 16 + r) * TOK + c];
+      for (int ww = 0; ww < NW; ++ww) v += part[ww * 16 * TOK + e];
       if (n < a.N && m < a.M) a.y[(size_t)m * a.N + n] = v * xs_s[c];
     }
     __syncthreads();
