@@ -410,15 +410,15 @@ bool want_mma(const lbc_params *p, int fmt, int M, int N, int Kp) {
 }
 
 // W4A8 on mma.sync.m16n8k32 s8 (gemv_i8mma.cu): 8 or 16 tokens per pass
-// (n-blocks of 8), nr = warps per CTA (4 or 8; default 8), nb = CTAs per SM
-// (default: up to 4, as many as fit)
+// (n-blocks of 8; up to 64 tokens in passes), nr = warps per CTA (4 or 8;
+// default 8), nb = CTAs per SM (default: up to 4, as many as fit)
 struct I8Plan {
   int nb = 1, nw = 8, passes = 1, grid = 1, smem = 0, cps = 1;
 };
 
 int plan_i8mma(int M, int N, int Kp, const lbc_params *p, I8Plan &P) {
   const DevInfo di = dev_info();
-  if (M > 16) return fail(LBC_ERR_PARAMS, "w4a8 mma path: at most 16 tokens");
+  if (M > 64) return fail(LBC_ERR_PARAMS, "w4a8 mma path: at most 64 tokens");
   P.nb = M <= 8 ? 1 : 2;
   P.passes = ceil_div(M, 8 * P.nb);
   P.nw = (p && p->nr > 0) ? p->nr : 8;
@@ -432,16 +432,18 @@ int plan_i8mma(int M, int N, int Kp, const lbc_params *p, I8Plan &P) {
   return 0;
 }
 
-// The int8 MMA kernel serves W4A8 on request (isa = LBC_PATH_MMA) and,
-// automatically with default tiling, 8-16 tokens, and 3-7 tokens whose rows
-// are too long for the decode kernel (measured on the BASELINE shapes: 1.2-2x
-// over the decode / staged / tcgen05 kernels there; the decode kernel stays
-// faster at 1-4 tokens on rows it takes)
+// The int8 MMA kernel serves W4A8 on request (isa = LBC_PATH_MMA, up to 64
+// tokens) and, automatically with default tiling, 8-63 tokens, and 3-7
+// tokens whose rows are too long for the decode kernel. Measured on the
+// BASELINE shapes: 1.2-2x over the decode / staged kernels at 8-16 tokens,
+// 2-3.5x over the staged / tcgen05 exact kernels at 17-63 (passes of 16
+// tokens re-read weights that are still in L2). The decode kernel stays
+// faster at 1-4 tokens on rows it takes, the prefill kernel from 64 tokens.
 bool want_i8mma(const lbc_params *p, int M, int N, int Kp) {
   (void)N;
   if (p && p->isa == LBC_PATH_MMA) return true;
   if (!path_auto(p) || (p && (p->mr > 0 || p->nr > 0 || p->kb > 0 || p->order > 0))) return false;
-  if (M < 3 || M > 16 || lbc::i8mma_smem(M <= 8 ? 1 : 2, 8, Kp) > dev_info().smem_optin) return false;
+  if (M < 3 || M > 63 || lbc::i8mma_smem(M <= 8 ? 1 : 2, 8, Kp) > dev_info().smem_optin) return false;
   return M >= 8 || !rows_eligible(lbc::FMT_W4A8, M, Kp, p);
 }
 
@@ -849,7 +851,7 @@ int lbc_gemm_w4a8(const float *x, int M, int Kp, const uint8_t *qw, const float 
                   const uint8_t *zeros, int N, float *y, const lbc_params *p, void *workspace,
                   void *stream) {
   if (int rc = check_shape(M, Kp, N, LBC_GROUP)) return rc;
-  if (p && p->isa == LBC_PATH_MMA && M > 16) return fail(LBC_ERR_PARAMS, "w4a8 mma path: at most 16 tokens");
+  if (p && p->isa == LBC_PATH_MMA && M > 64) return fail(LBC_ERR_PARAMS, "w4a8 mma path: at most 64 tokens");
   if (!x || !qw || !scales || !y || !al16(x) || !al16(qw))
     return fail(LBC_ERR_SHAPE, "NULL or misaligned pointer (x, qw need 16-byte alignment)");
   if (workspace && (reinterpret_cast<uintptr_t>(workspace) & 255u))

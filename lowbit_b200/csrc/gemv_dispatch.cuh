@@ -33,7 +33,7 @@ int rows_occupancy(int fmt, int mt, int ch, int r, int threads);
 // not instantiated): every CTA of the launch must be resident at once
 cudaError_t rows_gather_launch(const GemvArgs &a, int mt, int ch, int r, dim3 grid, int threads, cudaStream_t st);
 int rows_gather_occupancy(int mt, int ch, int r, int threads);
-// W4A8 with 1-16 tokens on mma.sync.m16n8k32 s8 (gemv_i8mma.cu): nb n-blocks
+// W4A8 with 1-64 tokens on mma.sync.m16n8k32 s8 (gemv_i8mma.cu): nb n-blocks
 // of 8 tokens per pass (grid.y passes), nw warps per CTA (nb, nw in {1, 2} x
 // {4, 8}); its dynamic shared memory and resident CTAs per SM
 cudaError_t i8mma_launch(const GemvArgs &a, int nb, int nw, dim3 grid, cudaStream_t st);

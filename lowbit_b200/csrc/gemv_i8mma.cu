@@ -1,5 +1,5 @@
-// W4A8 GEMM for 1-16 tokens on the tensor cores through
-// mma.sync.m16n8k32 (s8 x s8 -> s32).
+// W4A8 GEMM for 1-64 tokens (passes of up to 16, grid.y) on the tensor cores
+// through mma.sync.m16n8k32 (s8 x s8 -> s32).
 //
 // The reference's W4A8 arithmetic (src/lowbit/csrc/kern_vnni.c:30-72,
 // kern_scalar.c:49-59): y[m,n] = xs[m] * sum_g s[n,g] * (sum_{k in g} q*xq

@@ -6,7 +6,7 @@ Stage 1 picks the kernel path and the shape of the work: the automatic
 choice, then every alternative the planner accepts for the problem (for one
 or two tokens the register-streamed decode kernel at 2-8 CTAs per SM and the
 warp-level tensor-core kernel at several tilings (W4A16); for W4A8 with up
-to 16 tokens the int8 mma.sync kernel at 4 and 8 warps; for 3-63 tokens the
+to 64 tokens the int8 mma.sync kernel at 4 and 8 warps; for 3-63 tokens the
 tcgen05 exact kernel; from 64 tokens the exact kernel beside the bf16
 prefill kernel; below 64 tokens the staged SIMT kernel at every compiled
 tokens-per-pass x rows-per-team). Stage 2 refines the three fastest: pipeline
@@ -90,7 +90,7 @@ def _stage1(kind: str, m: int) -> list[K.Params]:
         if kind == "w4a16":                                      # warp-level tensor-core kernel
             c += [P(isa="mma", nr=nw, kb=kb, order=ns) for nw, kb, ns in
                   ((8, 4096, 2), (8, 2048, 4), (16, 4096, 3), (4, 2048, 4), (16, 2048, 4))]
-    if kind == "w4a8" and m <= 16:                               # int8 mma.sync kernel
+    if kind == "w4a8" and m <= 64:                               # int8 mma.sync kernel
         c += [P(isa="mma", nr=8), P(isa="mma", nr=4)]
     if m > 2:
         c.append(P(isa="tcgen05", mr=16))                        # tcgen05 exact kernel

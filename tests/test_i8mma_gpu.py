@@ -1,9 +1,9 @@
-"""W4A8 on mma.sync.m16n8k32 s8 (the automatic path for 8-16 tokens, or
-params isa="mma" for 1-16): A = q - z as s8 makes each 128-element group's
+"""W4A8 on mma.sync.m16n8k32 s8 (the automatic path for 8-63 tokens, or
+params isa="mma" for 1-64; passes of 16 tokens): A = q - z as s8 makes each 128-element group's
 int32 accumulator exactly the reference's sum(q * xq) - z * asum
 (src/lowbit/csrc/kern_scalar.c:49-59); the group scales fold it into fp32 in
 group order and the token scale comes last. Checked against the oracle with
-the reference's W4A8 bound for 1-16 tokens, ragged N, K from one group to
+the reference's W4A8 bound for 1-64 tokens, ragged N, K from one group to
 86, symmetric and asymmetric weights, extreme operands and every warp count
 and CTAs-per-SM setting; the int8-only entry point (gemm_w4a8_q) gives the
 same bits as the fp32 one."""
@@ -24,7 +24,7 @@ def _check(y, x, W):
                    R.w4a8_bound(xq, xs, asum, W.qw, W.scales, W.zeros), W8)
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 9, 16])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 9, 16, 17, 33, 64])
 @pytest.mark.parametrize("n,k", [(17, 128), (300, 384), (1000, 4096), (129, 11008)])
 @pytest.mark.parametrize("asym", [False, True])
 def test_i8mma_w4a8(m, n, k, asym):
@@ -64,7 +64,20 @@ def test_i8mma_extreme_operands():
     np.testing.assert_array_equal(y, R.gemm_w4a8_ref(xq, xs, asum, W.qw, W.scales, W.zeros).astype(np.float32))
 
 
-def test_i8mma_rejects_more_than_16_tokens():
+@pytest.mark.parametrize("m", [17, 40, 63])
+def test_i8mma_automatic_from_17_to_63_tokens(m):
+    """The automatic W4A8 path for 17-63 tokens (passes of 16), against the
+    oracle; the tcgen05 exact kernel stays reachable with isa="tcgen05"."""
+    rng = np.random.default_rng(m)
+    W = lb.quantize_int4(rng.standard_normal((700, 2048)).astype(np.float32), asym=True)
+    x = rng.standard_normal((m, 2048)).astype(np.float32)
+    assert K.describe_plan("w4a8", m, 700, W.kp)["kernel"] == "i8mma"
+    _check(K.gemm_w4a8(x, W), x, W)
+    assert K.describe_plan("w4a8", m, 700, W.kp, isa="tcgen05")["path"] == "tcgen05"
+    _check(K.gemm_w4a8(x, W, isa="tcgen05"), x, W)
+
+
+def test_i8mma_rejects_more_than_64_tokens():
     W = lb.quantize_int4(np.random.default_rng(2).standard_normal((64, 256)).astype(np.float32))
     with pytest.raises(ValueError):
-        K.gemm_w4a8(np.ones((17, 256), np.float32), W, K.Params(isa="mma"))
+        K.gemm_w4a8(np.ones((65, 256), np.float32), W, K.Params(isa="mma"))

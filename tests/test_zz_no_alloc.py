@@ -25,7 +25,7 @@ def _lib():
     return L
 
 
-def _run_both(L, x, W):
+def _run_both(L, x, W, isa=None):
     import torch
     dev = torch.device("cuda", torch.cuda.current_device())
     m, kp, n = x.shape[0], W.kp, W.n
@@ -40,21 +40,23 @@ def _run_both(L, x, W):
     ws = torch.empty(int(L.lbc_gemm_w4a8_workspace_size(m, kp)), dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream().cuda_stream
     zp = None if zz is None else zz.data_ptr()
+    p = None if isa is None else C.byref(K._params(None, isa))
     rc = L.lbc_gemm_w4a8(xd.data_ptr(), m, kp, qw.data_ptr(), sc.data_ptr(), zp, n, y_ref.data_ptr(),
-                         None, ws.data_ptr(), st)
+                         p, ws.data_ptr(), st)
     assert rc >= 0, L.lbc_last_error()
     rc = L.lbc_gemm_w4a8_noalloc(xd.data_ptr(), m, kp, qw.data_ptr(), sc.data_ptr(), zp, n,
-                                 y_na.data_ptr(), None, st)
+                                 y_na.data_ptr(), p, st)
     assert rc >= 0, L.lbc_last_error()
     torch.cuda.synchronize()
     return y_ref.cpu().numpy(), y_na.cpu().numpy()
 
 
-# (M, N, K, asym): the SIMT decode kernels (16 and 3 tokens) and, at 32 tokens
-# on a 4096 x 4096 matrix, the tensor-core exact kernel, whose partial-row
-# slots and epoch flags also live in the static scratch
-CASES = [(16, 256, 4096, False), (3, 96, 640, True), (32, 4096, 4096, True), (16, 256, 4096, False),
-         (32, 4096, 4096, True)]
+# (M, N, K, asym, isa): the automatic paths (16 and 32 tokens: the int8 mma
+# kernel; 3 tokens: the SIMT decode kernel) and, asked for explicitly at 32
+# tokens on a 4096 x 4096 matrix, the tensor-core exact kernel, whose
+# partial-row slots and epoch flags also live in the static scratch
+CASES = [(16, 256, 4096, False, None), (3, 96, 640, True, None), (32, 4096, 4096, True, "tcgen05"),
+         (16, 256, 4096, False, None), (32, 4096, 4096, True, "tcgen05"), (32, 4096, 4096, True, None)]
 
 
 def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
@@ -62,10 +64,10 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     rng = np.random.default_rng(99)
     # different problems in a row: each reuses (and must not depend on) what
     # the one before left in the static scratch
-    for (m, n, k, asym) in CASES:
+    for (m, n, k, asym, isa) in CASES:
         x = (rng.standard_normal((m, k)) * rng.uniform(0.1, 10)).astype(np.float32)
         W = lb.quantize_int4(rng.standard_normal((n, k)).astype(np.float32), asym=asym)
-        y_ref, y_na = _run_both(L, x, W)
+        y_ref, y_na = _run_both(L, x, W, isa)
         a = lb.quantize_act_int8(x)
         bound = R.w4a8_bound(a.xq, a.scale, a.gsum, W.qw, W.scales, W.zeros)
         R.assert_close(y_na, y_ref.astype(np.float64), bound, RTOL)
@@ -91,17 +93,17 @@ def test_noalloc_allocates_nothing():
     dev = torch.device("cuda", torch.cuda.current_device())
     st = torch.cuda.current_stream().cuda_stream
     probs = []
-    for (m, n, k, asym) in CASES[:3]:
+    for (m, n, k, asym, isa) in CASES[:3]:
         W = lb.quantize_int4(rng.standard_normal((n, k)).astype(np.float32), asym=asym)
         xd = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to(dev)
         probs.append((m, n, k, xd, torch.from_numpy(W.qw).to(dev), torch.from_numpy(W.scales).to(dev),
                       None if W.zeros is None else torch.from_numpy(W.zeros).to(dev),
-                      torch.empty((m, n), device=dev)))
+                      torch.empty((m, n), device=dev), None if isa is None else C.byref(K._params(None, isa))))
 
     def round_():
-        for (m, n, k, xd, qw, sc, zz, y) in probs:
+        for (m, n, k, xd, qw, sc, zz, y, p) in probs:
             rc = L.lbc_gemm_w4a8_noalloc(xd.data_ptr(), m, k, qw.data_ptr(), sc.data_ptr(),
-                                         None if zz is None else zz.data_ptr(), n, y.data_ptr(), None, st)
+                                         None if zz is None else zz.data_ptr(), n, y.data_ptr(), p, st)
             assert rc >= 0, L.lbc_last_error()
         torch.cuda.synchronize()
 
